@@ -1,0 +1,339 @@
+"""Benchmark of the NVFP4 quantized-linear hot path on B200 (the fused MLP pair).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = ``tfimage.linear.swiglu_mlp`` on one image's rows: quantize X [4352, 3072] under the gate/up input
+scale, gate/up NVFP4 GEMM [16384, 3072] whose epilogue applies SwiGLU and writes NVFP4 rows, down NVFP4 GEMM
+[3072, 8192] -> bf16 [4352, 3072]; 657.13 GFLOP. Inputs are resident in HBM; L2 is flushed (a 256 MiB write)
+between steps, outside the per-step CUDA events. Under torchrun every rank runs its own image (independent seeds,
+no collective: weak scaling) and the result is whole-job TFLOP/s over the max per-rank time.
+
+``e2e`` runs the same public call with the step's input copied from pinned host memory and its output copied back
+inside the timed region. ``cpu_baseline`` (rank 0, N=1) and ``--impl reference`` time the reference's torch CPU
+path -- oracle quantize, dequantize, fp32 matmul -- restated in ``oracle/`` on a bounded row sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "qwen-image21-tensorfold-rtx_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "NVFP4 linear TFLOP/s (% FP4 peak); DiT step ms @4096 tok; img/s at 1-8 GPU"
+M_ROWS, K_DIM, F_DIM = 4352, 3072, 8192
+FLOP_GU = 2 * M_ROWS * K_DIM * 2 * F_DIM          # 438.09 GFLOP
+FLOP_DOWN = 2 * M_ROWS * F_DIM * K_DIM            # 219.04 GFLOP
+FLOP_STEP = FLOP_GU + FLOP_DOWN
+FP4_TO_BF16 = 4.0                                  # B200 dense FP4 : BF16 tensor rate (9 : 2.25 PFLOP/s)
+# DRAM bytes per gate/up launch (dram__bytes_read.sum + dram__bytes_write.sum) from the ncu capture summarised in
+# profiles/gemm_nvfp4_swiglu_config1.md; None until measured.
+TRAFFIC_GU = None
+WORKLOAD = ("configs[1] fused NVFP4 MLP pair: X bf16 [4352,3072] N(0,1) -> gate/up W [16384,3072] N(0,0.02) with "
+            "SwiGLU->NVFP4 epilogue -> down W [3072,8192] N(0,0.02) -> bf16 [4352,3072]")
+
+
+def peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "sm_max_mhz": 1965.0}, \
+            "fallback"
+
+
+# ------------------------------------------------------------------------------------------------ clock sampling
+REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+           0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+           0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    """NVML SM clock + throttle reasons sampled every ~5 ms on a background thread."""
+
+    def __init__(self, index: int):
+        self.index, self.samples, self.reasons, self.max_mhz = index, [], 0, None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:                                   # noqa: BLE001 -- no NVML: report no clocks
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:                               # noqa: BLE001
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def report(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        names = [n for b, n in REASONS.items() if self.reasons & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------------------------------------ CPU baseline
+def cpu_reference_setup(seed: int = 0):
+    """The reference's CPU path: oracle-quantized weights, dequantized once (a weight cache), as fp32 torch."""
+    import numpy as np
+    import torch
+
+    from oracle import nvfp4 as onv
+
+    g = torch.Generator().manual_seed(seed)
+    wgu = (torch.randn(2 * F_DIM, K_DIM, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+    wd = (torch.randn(K_DIM, F_DIM, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+    out = {}
+    for name, w in (("gu", wgu), ("down", wd)):
+        gw = onv.weight_global(np.abs(w).max())
+        c, s = onv.quantize(w, gw)
+        out[name] = torch.from_numpy(onv.dequantize(c, s, gw))
+    x = torch.randn(M_ROWS, K_DIM, generator=g).to(torch.bfloat16).float().numpy()
+    out["x"] = x
+    out["act_x"] = onv.dynamic_act_global(np.abs(x).max())
+    return out
+
+
+def cpu_reference_step(st, rows: int, row0: int = 0):
+    """quantize+dequantize X rows -> fp32 matmul gate/up -> bf16 -> SwiGLU -> quantize+dequantize under down.act ->
+    fp32 matmul down -> bf16 (tools/gemm_tf.py:21-24,43; kernels.py:80)."""
+    import numpy as np
+    import torch
+
+    from oracle import fusions as ofu
+    from oracle import nvfp4 as onv
+
+    xs = st["x"][row0:row0 + rows]
+    xd = torch.from_numpy(onv.dequantize(*onv.quantize(xs, st["act_x"]), st["act_x"]))
+    gu = onv.bf16_round((xd @ st["gu"].T).numpy())
+    h = ofu.swiglu(gu)
+    act_h = st.setdefault("act_h", 4 * float(np.abs(h).max()) / (6 * 448))
+    hd = torch.from_numpy(onv.dequantize(*onv.quantize(h, act_h), act_h))
+    return onv.bf16_round((hd @ st["down"].T).numpy())
+
+
+def cpu_baseline(budget_s: float = 10.0, rows: int = 64):
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    st = cpu_reference_setup()
+    cpu_reference_step(st, rows)                                      # warm-up, sets act_h
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu_reference_step(st, rows, row0=(n * rows) % (M_ROWS - rows))
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = (time.perf_counter() - t0) / n
+    flop = FLOP_STEP * rows / M_ROWS
+    return {"value": flop / dt / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{rows} of the {M_ROWS} rows per step, {n} steps over {budget_s:.0f} s: oracle NVFP4 "
+                      f"quantize+dequantize, torch fp32 matmul, SwiGLU, requantize, fp32 matmul (weights "
+                      f"dequantized once outside the timing)"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    st = cpu_reference_setup()
+    t0 = time.perf_counter()
+    cpu_reference_step(st, 16)
+    probe = max(time.perf_counter() - t0, 1e-3)
+    per_row = probe / 16
+    rows = int(max(8, min(M_ROWS // 2, (120.0 / max(args.steps + args.warmup, 1)) / per_row)))
+    for i in range(args.warmup):
+        cpu_reference_step(st, rows, row0=(i * rows) % (M_ROWS - rows))
+    times = []
+    for i in range(args.steps):
+        t0 = time.perf_counter()
+        cpu_reference_step(st, rows, row0=(i * rows) % (M_ROWS - rows))
+        times.append(time.perf_counter() - t0)
+    dt = sum(times) / len(times)
+    value = FLOP_STEP * rows / M_ROWS / dt / 1e12
+    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (dequantized nvfp4)", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "rows_per_step": rows, "M": M_ROWS, "K": K_DIM, "F": F_DIM},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"{rows} of {M_ROWS} rows per step (reference torch CPU dequant-matmul "
+                                       f"path restated in oracle/)"},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------------ our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    from tfimage import _lib
+    from tfimage import kernels as Kn
+    from tfimage import linear as L
+
+    # ------------------------------------------------------------------ synthetic model + calibrated scales
+    g = torch.Generator().manual_seed(1000 + rank)
+    wgu = (torch.randn(2 * F_DIM, K_DIM, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    wd = (torch.randn(K_DIM, F_DIM, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    x_host = torch.randn(M_ROWS, K_DIM, generator=g).to(torch.bfloat16).pin_memory()
+    x = x_host.to(dev)
+    gate_up, down = L.Nvfp4Linear(wgu), L.Nvfp4Linear(wd)
+    del wgu, wd
+    gate_up.set_act(float(_lib.absmax(x)) / (6 * 448))             # activation global = amax / (6 * 448)
+    h = Kn.swiglu(gate_up(x))
+    down.set_act(4 * float(_lib.absmax(h)) / (6 * 448))             # calibrate.py's 4x margin
+    del h
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev):
+        ev[0].record(stream)
+        q = gate_up.quantize(x)
+        ev[1].record(stream)
+        hc, hs = _lib.gemm_nvfp4_swiglu(q.codes, q.sf, gate_up.lin.codes, gate_up.lin.bs, M_ROWS, F_DIM, K_DIM,
+                                        q.act * gate_up.lin.scale, down.lin.act)
+        ev[2].record(stream)
+        y = _lib.gemm_nvfp4(hc, hs, down.lin.codes, down.lin.bs, M_ROWS, K_DIM, F_DIM,
+                            down.lin.act * down.lin.scale)
+        ev[3].record(stream)
+        return y
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step([torch.cuda.Event(enable_timing=True) for _ in range(4)])
+        flush.zero_()
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    barrier()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            step(events[i])
+            flush.zero_()
+        barrier()
+    per = [[e[j].elapsed_time(e[j + 1]) for j in range(3)] for e in events]      # ms: quant, gate/up, down
+    step_ms = [sum(p) for p in per]
+    tot = torch.tensor([sum(step_ms), sum(p[1] for p in per)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    ms_step = float(tot[0]) / args.steps
+    value = world * FLOP_STEP / (ms_step * 1e-3) / 1e12
+
+    # --------------------------------------------------------------------------------- end to end (host buffers)
+    y_host = torch.empty((M_ROWS, K_DIM), dtype=torch.bfloat16).pin_memory()
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(max(3, min(args.steps, 50)))]
+    for _ in range(2):
+        xd = x_host.to(dev, non_blocking=True)
+        y_host.copy_(L.swiglu_mlp(gate_up, down, xd), non_blocking=True)
+    barrier()
+    for a, b in e2e_ev:
+        flush.zero_()
+        a.record(stream)
+        xd = x_host.to(dev, non_blocking=True)
+        y_host.copy_(L.swiglu_mlp(gate_up, down, xd), non_blocking=True)
+        b.record(stream)
+    barrier()
+    e2e_t = torch.tensor([sum(a.elapsed_time(b) for a, b in e2e_ev) / len(e2e_ev)], dtype=torch.float64,
+                         device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_value = world * FLOP_STEP / (float(e2e_t[0]) * 1e-3) / 1e12
+    status = _lib.device_status()
+
+    if rank == 0:
+        pk, src = peaks()
+        fp4_peak = FP4_TO_BF16 * pk["bf16_tflops"]
+        gu_ms = statistics.median(p[1] for p in per)
+        down_ms = statistics.median(p[2] for p in per)
+        q_ms = statistics.median(p[0] for p in per)
+        achieved = FLOP_GU / (gu_ms * 1e-3) / 1e12
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "nvfp4", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "M": M_ROWS, "K": K_DIM, "F": F_DIM, "global_batch": world,
+                       "rows_per_gpu": M_ROWS, "parallelism": f"dp{world} (independent images, no collective)",
+                       "l2": "flushed between steps: 256 MiB write outside the per-step events"},
+            "pct_fp4_peak": value / world / fp4_peak,
+            "kernels_ms": {"quant_x": q_ms, "gate_up_swiglu_nvfp4": gu_ms, "down": down_ms},
+            "roofline": {"bound": "tensor", "kernel": "gemm_kernel<MODE_FP4_SWIGLU> (gate/up + SwiGLU->NVFP4)",
+                         "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s", "frac": achieved / fp4_peak,
+                         "traffic": TRAFFIC_GU,
+                         "peak_note": f"dense FP4 = {FP4_TO_BF16:g} x bf16 burst {pk['bf16_tflops']} TFLOP/s "
+                                      f"({src}); nominal 9000"},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": x_host.numel() * 2,
+                    "d2h_bytes_per_step": y_host.numel() * 2},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clk.report(),
+            "device_status": status,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,129 @@
+/*
+ * libtfb -- sm_100a (B200) kernels behind tfimage's quantized-linear API, as a plain C ABI.
+ *
+ * Conventions (every entry point):
+ *   - all buffers are caller-owned device pointers; nothing here allocates device memory;
+ *   - work is enqueued on the caller's stream (`stream` is a cudaStream_t passed as void*; NULL = legacy default);
+ *   - no entry point synchronizes except tfb_device_status();
+ *   - the return value is a tfb_status; on failure tfb_last_error() (thread-local) explains it;
+ *   - shapes/alignments are validated before any launch (TFB_BAD_SHAPE / TFB_BAD_ALIGN), the device must be
+ *     compute capability 10.0 (TFB_BAD_ARCH);
+ *   - GEMM kernels bound every pipeline wait; a wait that runs out records a code that tfb_device_status()
+ *     returns (TFB_DEVICE_TIMEOUT) instead of hanging the GPU.
+ *
+ * Formats:
+ *   bf16       -- raw 16-bit bfloat16 bit patterns;
+ *   NVFP4      -- codes: uint8 [rows, K/2], two E2M1 values per byte, even element in the low nibble;
+ *                 scales: one E4M3 byte per 16 K-elements, either row-major [rows, K/16] (TFB_SF_ROWS) or the
+ *                 GEMM layout TFB_SF_TILED: 512-byte chunks [ceil(rows/128)][K/64][512] where row r, scale j of a
+ *                 chunk sits at (r%32)*16 + ((r%128)/32)*4 + (j%4); rows past the end are zero;
+ *                 global: an fp32 per-tensor scale g, value = lut[code] * e4m3(scale) * g.
+ *   FP8        -- E4M3 bytes [rows, K].
+ */
+#ifndef TFB_H
+#define TFB_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  TFB_OK = 0,
+  TFB_BAD_SHAPE = 1,
+  TFB_BAD_ALIGN = 2,
+  TFB_BAD_ARCH = 3,
+  TFB_DEVICE_TIMEOUT = 4,
+  TFB_CUDA_ERR = 5,
+  TFB_BAD_ARG = 6
+} tfb_status;
+
+enum { TFB_SF_ROWS = 0, TFB_SF_TILED = 1 };
+
+/* Library version (major*10000 + minor*100 + patch). */
+int tfb_version(void);
+
+/* Message for the last failing call on this host thread ("" if none). */
+const char* tfb_last_error(void);
+
+/* Bytes of a TFB_SF_TILED scale buffer for `rows` x `k` elements. */
+int64_t tfb_sf_tiled_bytes(int64_t rows, int64_t k);
+
+/* Synchronizes the current device and reads (and, if reset != 0, clears) the device-side error word set by a
+ * kernel whose bounded wait ran out: *code = 0 when clean. Returns TFB_DEVICE_TIMEOUT when *code != 0. */
+tfb_status tfb_device_status(int* code, int reset);
+
+/* amax = max |x| over n bf16 values, written to *amax_dev (fp32, device).
+ * Replaces the device half of `float(x.abs().amax())` in Nvfp4Linear.__call__ (tfimage/linear.py:127). */
+tfb_status tfb_absmax_bf16(const void* x, int64_t n, float* amax_dev, void* stream);
+
+/* Dynamic FP8 activation scale on the device: *a_dev = max(amax(x) / 448, 1e-12) (fp32).
+ * Replaces Fp8Linear._act (tfimage/linear.py:84-89). */
+tfb_status tfb_fp8_act_scale(const void* x, int64_t n, float* a_dev, void* stream);
+
+/* NVFP4 row quantizer: x bf16 [M, K] (row stride ldx elements) under global g -> codes [M, K/2] + scales.
+ * Replaces TensorFold checkpoint.quant4 (called at tfimage/linear.py:36 and tools/gemm_tf.py:17,45).
+ * K % 64 == 0 (K % 16 == 0 for TFB_SF_ROWS). */
+tfb_status tfb_quant_nvfp4(const void* x, int64_t M, int64_t K, int64_t ldx, float global, uint8_t* codes,
+                           uint8_t* sf, int sf_layout, void* stream);
+
+/* FP8 activation quantizer: q[m, k] = e4m3(clamp(x / *a_dev, -448, 448)) (tfimage/linear.py:95). q is [M, K]. */
+tfb_status tfb_quant_fp8(const void* x, int64_t M, int64_t K, int64_t ldx, const float* a_dev, uint8_t* q,
+                         void* stream);
+
+/* W4A4 NVFP4 GEMM on tcgen05 block-scaled FP4 MMA: y[M, N] = bf16(alpha * sum_k deq(a)[m,k] * deq(b)[n,k])
+ * with deq() excluding the globals (alpha = g_a * g_b). Scales in TFB_SF_TILED layout.
+ * Replaces TensorFold checkpoint.prompt(A4, ...) after quantization (tfimage/linear.py:130). K % 128 == 0,
+ * N % 32 == 0, ldy % 8 == 0. */
+tfb_status tfb_gemm_nvfp4(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* b_codes, const uint8_t* b_sf,
+                          int64_t M, int64_t N, int64_t K, float alpha, void* y, int64_t ldy, void* stream);
+
+/* W8A8 FP8 GEMM on tcgen05 kind::f8f6f4: y[M, N] = bf16(sum_k a[m,k] b[n,k] * a_scale * b_scale[n or 0]).
+ * Scales are device fp32 (a_scale: one value; b_scale: N values if b_per_channel else one). Replaces
+ * torch._scaled_mm in Fp8Linear.__call__ (tfimage/linear.py:98); M is ragged (no padding). K % 128 == 0,
+ * N % 32 == 0. */
+tfb_status tfb_gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, int64_t K, const float* a_scale,
+                        const float* b_scale, int b_per_channel, void* y, int64_t ldy, void* stream);
+
+/* Gate/up NVFP4 GEMM with a SwiGLU epilogue that writes NVFP4: W_gu = [gate; up] codes [2F, K].
+ * h = bf16(bf16(silu(gate)) * up) with gate/up = bf16(alpha * acc), quantized under h_global into
+ * h_codes [M, F/2] and h_sf (TFB_SF_TILED, rows = M, K = F). gu_out (nullable) receives the bf16 gate/up
+ * [M, 2F] for testing. Replaces the first half of TensorFold checkpoint.mlp_prompt (tfimage/linear.py:150).
+ * F % 128 == 0, K % 128 == 0. */
+tfb_status tfb_gemm_nvfp4_swiglu(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* gu_codes,
+                                 const uint8_t* gu_sf, int64_t M, int64_t F, int64_t K, float alpha, float h_global,
+                                 uint8_t* h_codes, uint8_t* h_sf, void* gu_out, void* stream);
+
+/* Whole fused MLP pair (tfimage/linear.py:136-150, swiglu_mlp): quantize x [M, K] under act_x, gate/up GEMM with
+ * the SwiGLU->NVFP4 epilogue under act_h, down GEMM -> y [M, K] bf16. The four ws_* buffers are caller-owned
+ * scratch: ws_xc [M, K/2], ws_xsf tfb_sf_tiled_bytes(M, K), ws_hc [M, F/2], ws_hsf tfb_sf_tiled_bytes(M, F). */
+tfb_status tfb_mlp_nvfp4(const void* x, int64_t M, int64_t K, int64_t F, float act_x, const uint8_t* gu_codes,
+                         const uint8_t* gu_sf, float g_gu, const uint8_t* down_codes, const uint8_t* down_sf,
+                         float g_down, float act_h, void* y, uint8_t* ws_xc, uint8_t* ws_xsf, uint8_t* ws_hc,
+                         uint8_t* ws_hsf, void* stream);
+
+/* AdaLN modulate: per row of x [B*N, D] (batch b = row / N): y = LN(x) * (1 + scale[b]) (+ shift[b]), fp32
+ * inside, eps inside the rsqrt; scale/shift are fp32 [B, D] (shift nullable). Outputs (each nullable, at least
+ * one): out bf16 [B*N, D]; NVFP4 codes [B*N, D/2] + tiled scales of the bf16-rounded result under q_global.
+ * Replaces the Triton _adaln_kernel (tfimage/kernels.py:14-37). D % 256 == 0, D <= 8192. */
+tfb_status tfb_adaln(const void* x, int64_t B, int64_t N, int64_t D, const float* scale, const float* shift,
+                     float eps, void* out, float q_global, uint8_t* codes, uint8_t* sf, void* stream);
+
+/* RMSNorm over the head dim (weight w, fp32 [D]) then RoPE on interleaved pairs with cos/sin fp32 [N, D/2], per
+ * (b, n, h): src element (b, n, h, d) at src + b*src_sb + n*src_sn + src_off + h*D + d; dst at
+ * dst + b*dst_sb + n*dst_sn + h*D + d (element strides; dst may be a row slice of a larger buffer).
+ * Replaces the Triton _rms_rope_kernel (tfimage/kernels.py:40-70). D == 128. */
+tfb_status tfb_rms_rope(const void* src, int64_t B, int64_t N, int64_t H, int64_t D, int64_t src_sb, int64_t src_sn,
+                        int64_t src_off, const float* w, const float* cos, const float* sin, float eps, void* dst,
+                        int64_t dst_sb, int64_t dst_sn, void* stream);
+
+/* Standalone SwiGLU: gu bf16 [M, 2F] = [gate | up] -> out bf16 [M, F] = bf16(bf16(silu(gate)) * up).
+ * Replaces the Triton _swiglu_kernel (tfimage/kernels.py:73-92). F % 8 == 0. */
+tfb_status tfb_swiglu(const void* gu, int64_t M, int64_t F, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TFB_H */

@@ -1,0 +1,233 @@
+// Fused elementwise kernels of a DiT block: AdaLN modulate (+ NVFP4 quantize), RMSNorm + RoPE, SwiGLU.
+// All are HBM-bound: 16-byte coalesced loads/stores, statistics in fp32 registers, one pass over the input.
+#include "tfb_common.cuh"
+
+namespace tfb {
+namespace {
+
+// ------------------------------------------------------------------------------------------------------- AdaLN
+// One warp per row. Lane l holds columns i*256 + l*8 .. +7 for chunks i < NCH (D = 256 * NCH), so every load and
+// store of a warp covers 512 contiguous bytes. A 16-element quantization block is the lane pair (2q, 2q+1).
+constexpr int kAdaWarps = 8;
+
+template <int NCH>
+__global__ void __launch_bounds__(kAdaWarps * 32) adaln_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
+                                                               int64_t rows_total, int64_t rows_per_b,
+                                                               const float* __restrict__ scale,
+                                                               const float* __restrict__ shift, float eps,
+                                                               __nv_bfloat16* __restrict__ out, float qg,
+                                                               uint8_t* __restrict__ codes, uint8_t* __restrict__ sf) {
+  constexpr int D = NCH * 256;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = blockIdx.x * (int64_t)kAdaWarps + (threadIdx.x >> 5);
+  if (row >= rows_total) return;
+  if (row >= rows) {  // padding rows of the tiled scale layout: zero scales
+    if (sf && (lane & 7) == 0)
+      for (int i = 0; i < NCH; ++i)
+        *reinterpret_cast<uint32_t*>(sf + sf_tiled_offset(row, i * 16 + (lane >> 1), D >> 6)) = 0u;
+    return;
+  }
+  float v[NCH][8];
+  const __nv_bfloat16* xr = x + row * D;
+  float sum = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) {
+    unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(xr + i * 256 + lane * 8)), v[i]);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) sum += v[i][k];
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum / D;
+  float var = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NCH; ++i)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      v[i][k] -= mean;
+      var += v[i][k] * v[i][k];
+    }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+  const float rstd = rsqrtf(var / D + eps);
+  const int64_t b = row / rows_per_b;
+  const float* sc = scale + b * D;
+  const float* sh = shift ? shift + b * D : nullptr;
+  const Nvfp4Enc enc = nvfp4_enc(qg);
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) {
+    const int c0 = i * 256 + lane * 8;
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(sc + c0));
+    const float4 s1 = __ldg(reinterpret_cast<const float4*>(sc + c0 + 4));
+    float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    float y[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) y[k] = v[i][k] * rstd * (1.0f + s[k]);
+    if (sh) {
+      const float4 h0 = __ldg(reinterpret_cast<const float4*>(sh + c0));
+      const float4 h1 = __ldg(reinterpret_cast<const float4*>(sh + c0 + 4));
+      const float h[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+      for (int k = 0; k < 8; ++k) y[k] += h[k];
+    }
+    uint4 packed = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
+                              pack_bf16x2(y[6], y[7]));
+    if (out) *reinterpret_cast<uint4*>(out + row * D + c0) = packed;
+    if (codes) {
+      float q[8];
+      unpack_bf16x8(packed, q);  // quantize the bf16-rounded result
+      float amax = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(q[k]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      const uint32_t sfb = nvfp4_scale(amax, enc);
+      *reinterpret_cast<uint32_t*>(codes + row * (D >> 1) + (c0 >> 1)) = nvfp4_codes8(q, nvfp4_inv(sfb, enc));
+      // lanes 8t, 8t+2, 8t+4, 8t+6 hold blocks 4t..4t+3 of this chunk: one 32-bit word of the tiled layout
+      const uint32_t b1 = __shfl_down_sync(0xffffffffu, sfb, 2);
+      const uint32_t b2 = __shfl_down_sync(0xffffffffu, sfb, 4);
+      const uint32_t b3 = __shfl_down_sync(0xffffffffu, sfb, 6);
+      if ((lane & 7) == 0)
+        *reinterpret_cast<uint32_t*>(sf + sf_tiled_offset(row, i * 16 + (lane >> 1), D >> 6)) =
+            sfb | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    }
+  }
+}
+
+template <int NCH>
+void launch_adaln(const void* x, int64_t rows, int64_t rows_total, int64_t rows_per_b, const float* scale,
+                  const float* shift, float eps, void* out, float qg, uint8_t* codes, uint8_t* sf, cudaStream_t s) {
+  const int64_t grid = (rows_total + kAdaWarps - 1) / kAdaWarps;
+  adaln_kernel<NCH><<<grid, kAdaWarps * 32, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, rows_total, rows_per_b,
+                                                    scale, shift, eps, static_cast<__nv_bfloat16*>(out), qg, codes,
+                                                    sf);
+}
+
+// --------------------------------------------------------------------------------------------- RMSNorm + RoPE
+// Half a warp per (b, n, h) with D = 128: lane holds 8 elements (four interleaved pairs), 16-byte accesses.
+__global__ void __launch_bounds__(256) rms_rope_kernel(const __nv_bfloat16* __restrict__ src, int64_t units, int64_t N,
+                                                       int64_t H, int64_t src_sb, int64_t src_sn, int64_t src_off,
+                                                       const float* __restrict__ w, const float* __restrict__ cosp,
+                                                       const float* __restrict__ sinp, float eps,
+                                                       __nv_bfloat16* __restrict__ dst, int64_t dst_sb,
+                                                       int64_t dst_sn) {
+  constexpr int D = 128;
+  const int64_t unit = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 4;
+  const int l = threadIdx.x & 15;
+  const bool live = unit < units;
+  const int64_t uu = live ? unit : 0;
+  const int64_t h = uu % H, bn = uu / H, n = bn % N, b = bn / N;
+  float x[8];
+  unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(src + b * src_sb + n * src_sn + src_off + h * D + l * 8)), x);
+  float ss = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) ss += x[k] * x[k];
+#pragma unroll
+  for (int o = 8; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rr = rsqrtf(ss / D + eps);
+  const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + l * 8));
+  const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + l * 8 + 4));
+  const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  const float4 c = __ldg(reinterpret_cast<const float4*>(cosp + n * (D / 2) + l * 4));
+  const float4 s = __ldg(reinterpret_cast<const float4*>(sinp + n * (D / 2) + l * 4));
+  const float cv[4] = {c.x, c.y, c.z, c.w}, sv[4] = {s.x, s.y, s.z, s.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float x0 = x[2 * p] * rr * wv[2 * p], x1 = x[2 * p + 1] * rr * wv[2 * p + 1];
+    o[p] = pack_bf16x2(cv[p] * x0 - sv[p] * x1, sv[p] * x0 + cv[p] * x1);
+  }
+  if (live)
+    *reinterpret_cast<uint4*>(dst + b * dst_sb + n * dst_sn + h * D + l * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// ------------------------------------------------------------------------------------------------------ SwiGLU
+// bf16(bf16(silu(g)) * u), 8 columns per thread.
+__global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __restrict__ gu, int64_t M, int64_t F,
+                                                     __nv_bfloat16* __restrict__ out) {
+  const int64_t per_row = F >> 3;
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (t >= M * per_row) return;
+  const int64_t m = t / per_row, c = (t - m * per_row) * 8;
+  float g[8], u[8];
+  unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(gu + m * 2 * F + c)), g);
+  unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(gu + m * 2 * F + F + c)), u);
+  float y[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) y[k] = bf16_round(__fdiv_rn(g[k], 1.0f + expf(-g[k]))) * u[k];
+  *reinterpret_cast<uint4*>(out + m * F + c) =
+      make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+}
+
+}  // namespace
+}  // namespace tfb
+
+extern "C" {
+
+tfb_status tfb_adaln(const void* x, int64_t B, int64_t N, int64_t D, const float* scale, const float* shift, float eps,
+                     void* out, float q_global, uint8_t* codes, uint8_t* sf, void* stream) {
+  using namespace tfb;
+  const DeviceInfo* di;
+  tfb_status st = device_info(&di);
+  if (st != TFB_OK) return st;
+  if (B <= 0 || N < 0 || D <= 0 || D % 256 || D > 8192)
+    return fail(TFB_BAD_SHAPE, "adaln: need D %% 256 == 0 and D <= 8192 (D=%lld)", (long long)D);
+  if (!out && !codes) return fail(TFB_BAD_ARG, "adaln: no output requested");
+  if ((codes == nullptr) != (sf == nullptr)) return fail(TFB_BAD_ARG, "adaln: codes and scales go together");
+  if (codes && (!(q_global > 0.0f) || !isfinite(q_global)))
+    return fail(TFB_BAD_ARG, "adaln: quantization global must be positive and finite");
+  if (!aligned(x, 16) || (out && !aligned(out, 16)) || !aligned(scale, 16) || (shift && !aligned(shift, 16)) ||
+      (codes && (!aligned(codes, 4) || !aligned(sf, 4))))
+    return fail(TFB_BAD_ALIGN, "adaln: x/out/scale/shift must be 16-byte aligned");
+  const int64_t rows = B * N;
+  const int64_t rows_total = codes ? (rows + 127) / 128 * 128 : rows;
+  if (rows_total == 0) return TFB_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (D / 256) {
+#define TFB_ADA(n) \
+  case n: launch_adaln<n>(x, rows, rows_total, N, scale, shift, eps, out, q_global, codes, sf, s); break;
+    TFB_ADA(1) TFB_ADA(2) TFB_ADA(3) TFB_ADA(4) TFB_ADA(6) TFB_ADA(8) TFB_ADA(12) TFB_ADA(16) TFB_ADA(24) TFB_ADA(32)
+#undef TFB_ADA
+    default:
+      return fail(TFB_BAD_SHAPE, "adaln: D=%lld not instantiated (256 x {1,2,3,4,6,8,12,16,24,32})", (long long)D);
+  }
+  TFB_CUDA(cudaGetLastError());
+  return TFB_OK;
+}
+
+tfb_status tfb_rms_rope(const void* src, int64_t B, int64_t N, int64_t H, int64_t D, int64_t src_sb, int64_t src_sn,
+                        int64_t src_off, const float* w, const float* cos, const float* sin, float eps, void* dst,
+                        int64_t dst_sb, int64_t dst_sn, void* stream) {
+  using namespace tfb;
+  const DeviceInfo* di;
+  tfb_status st = device_info(&di);
+  if (st != TFB_OK) return st;
+  if (D != 128 || B < 0 || N < 0 || H <= 0) return fail(TFB_BAD_SHAPE, "rms_rope: head dim must be 128");
+  if (!aligned(src, 16) || !aligned(dst, 16) || src_sb % 8 || src_sn % 8 || src_off % 8 || dst_sb % 8 ||
+      dst_sn % 8 || !aligned(w, 16) || !aligned(cos, 16) || !aligned(sin, 16))
+    return fail(TFB_BAD_ALIGN, "rms_rope: pointers and element strides must be 16-byte aligned");
+  const int64_t units = B * N * H;
+  if (units == 0) return TFB_OK;
+  const int64_t threads = units * 16;
+  rms_rope_kernel<<<(threads + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(src), units, N, H, src_sb, src_sn, src_off, w, cos, sin, eps,
+      static_cast<__nv_bfloat16*>(dst), dst_sb, dst_sn);
+  TFB_CUDA(cudaGetLastError());
+  return TFB_OK;
+}
+
+tfb_status tfb_swiglu(const void* gu, int64_t M, int64_t F, void* out, void* stream) {
+  using namespace tfb;
+  const DeviceInfo* di;
+  tfb_status st = device_info(&di);
+  if (st != TFB_OK) return st;
+  if (M < 0 || F <= 0 || F % 8) return fail(TFB_BAD_SHAPE, "swiglu: F must be a positive multiple of 8");
+  if (!aligned(gu, 16) || !aligned(out, 16)) return fail(TFB_BAD_ALIGN, "swiglu: buffers must be 16-byte aligned");
+  const int64_t threads = M * (F / 8);
+  if (threads == 0) return TFB_OK;
+  swiglu_kernel<<<(threads + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(gu), M, F, static_cast<__nv_bfloat16*>(out));
+  TFB_CUDA(cudaGetLastError());
+  return TFB_OK;
+}
+
+}  // extern "C"

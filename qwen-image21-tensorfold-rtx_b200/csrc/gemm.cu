@@ -1,0 +1,587 @@
+// tcgen05 GEMMs for sm_100a: NVFP4 W4A4 (kind::mxf4nvf4, E4M3 block scales per 16), FP8 W8A8 (kind::f8f6f4), and
+// the NVFP4 gate/up GEMM whose epilogue applies SwiGLU and writes NVFP4 rows + scales for the down projection.
+//
+// One persistent CTA per SM walks 128 x 256 output tiles. Warp roles (192 threads):
+//   warp 0 lane 0 : TMA producer -- A tile [128 rows x 128 B], B tile [256 rows x 128 B] (two 128-row boxes),
+//                   128-byte swizzle, plus the stage's scale chunks by 1-D bulk copies; STAGES-deep ring.
+//   warp 1        : allocates TMEM (512 columns); lane 0 issues tcgen05.cp (scales -> TMEM) and tcgen05.mma
+//                   (M=128, N=256, K=64 fp4 / 32 fp8 per instruction) into a 256-column fp32 accumulator.
+//   warps 2..5    : epilogue -- tcgen05.ld 32 columns at a time (warp w reads TMEM lanes 32*(w%4)..+31, one output
+//                   row per thread), scale, convert, store.
+// Every mbarrier wait is bounded (kWaitLimitNs); a wait that runs out records a code in the device error word,
+// the other roles see it and leave their loops, in-flight copies/MMAs are drained (bounded) and TMEM is freed.
+// No TMA multicast anywhere: each CTA loads its own operand tiles.
+#include "tfb_common.cuh"
+
+namespace tfb {
+namespace {
+
+constexpr int BM = 128, BN = 256, BKB = 128;  // tile rows, tile cols, K bytes per stage (and swizzle span)
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BKB;             // 16 KB
+constexpr int B_BYTES = BN * BKB;             // 32 KB
+constexpr int SFA_BYTES = 4 * 512;            // 4 scale chunks (64 K-elements each) of 128 rows
+constexpr int SFB_BYTES = 2 * 4 * 512;        // two 128-row groups
+constexpr int THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t ACC_COL = 0;               // accumulator: columns [0, 256)
+constexpr uint32_t SF_COL = 256;              // scales: 2 buffers x 48 columns (SFA 4x4, SFB 4x8)
+
+enum Mode { MODE_FP4 = 0, MODE_FP8 = 1, MODE_FP4_SWIGLU = 2 };
+
+struct Params {
+  int M, N;              // output rows / cols (swiglu: N = F, the hidden width)
+  int num_m, num_n, num_tiles;
+  int num_ks;            // pipeline stages along K
+  int kb_total;          // MMA k-blocks along K
+  int b_rows;            // rows of the B operand (N, or 2F for swiglu)
+  const uint8_t* sfa;    // tiled scales (fp4 modes)
+  const uint8_t* sfb;
+  int sf_chunks;         // K / 64
+  int sfb_groups;        // ceil(b_rows / 128)
+  void* y;
+  int64_t ldy;
+  float alpha;           // fp4: g_a * g_b
+  const float* a_scale;  // fp8
+  const float* b_scale;
+  int b_per_channel;
+  float h_g;             // swiglu: global of the NVFP4 output
+  uint8_t* h_codes;      // [M, F/2]
+  uint8_t* h_sf;         // tiled, K = F
+  __nv_bfloat16* gu_out; // optional [M, 2F]
+  int* err;
+};
+
+// ----------------------------------------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false if the limit ran out (code recorded) or another role already aborted.
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try(a, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try(a, parity)) return true;
+    if ((it & 255) == 0) {
+      if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+      if ((long long)(globaltimer() - t0) > kWaitLimitNs) {
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle: rows 128 B apart, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t desc_sw128(const void* p) {
+  const uint64_t a = smem_u32(p);
+  return ((a & 0x3FFFFull) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+// Descriptor of a 32-row x 16-byte scale block (no swizzle, 8-row core matrices 128 B apart) for tcgen05.cp.
+__device__ __forceinline__ uint64_t desc_sf(const void* p) {
+  const uint64_t a = smem_u32(p);
+  return ((a & 0x3FFFFull) >> 4) | (1ull << 16) | (8ull << 32) | (1ull << 46);
+}
+
+// Instruction descriptors (M = 128, N = 256, both operands K-major, fp32 accumulate).
+//   block-scaled mxf4nvf4: A/B format E2M1 (1) at bits 7-9 / 10-12, scale format UE4M3 (0) at bit 23;
+//   f8f6f4: D format F32 (1) at bits 4-5, A/B format E4M3 (0).
+constexpr uint32_t IDESC_FP4 = (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+constexpr uint32_t IDESC_FP8 = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_fp4(uint32_t d, uint64_t a, uint64_t b, uint32_t sfa, uint32_t sfb, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+      ::"r"(d), "l"(a), "l"(b), "r"(IDESC_FP4), "r"(acc), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+__device__ __forceinline__ void mma_fp8(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d), "l"(a), "l"(b), "r"(IDESC_FP8), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t desc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__host__ __device__ constexpr int smem_bytes(int mode) {
+  return 1024 /* alignment slack */ + STAGES * (A_BYTES + B_BYTES) +
+         (mode == MODE_FP8 ? 0 : STAGES * (SFA_BYTES + SFB_BYTES)) + 256 /* barriers + TMEM slot */;
+}
+
+// --------------------------------------------------------------------------------------------------- the kernel
+template <int MODE>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+  constexpr bool FP4 = MODE != MODE_FP8;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * A_BYTES;
+  uint8_t* sSFA = sB + STAGES * B_BYTES;
+  uint8_t* sSFB = sSFA + (FP4 ? STAGES * SFA_BYTES : 0);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + (FP4 ? STAGES * SFB_BYTES : 0));
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* drain = acc_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 128);
+    mbar_init(drain, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------------------------------------- producer
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+    int stage = 0;
+    uint32_t ph = 0;
+    uint32_t issued = 0;     // bit s: stage s was armed at least once
+    uint32_t last_ph = 0;    // bit s: parity of its last arming
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+      const int mb = tile % p.num_m, nb = tile / p.num_m;
+      int rb0, rb1;
+      if (MODE == MODE_FP4_SWIGLU) {
+        rb0 = nb * 128;
+        rb1 = p.N + nb * 128;
+      } else {
+        rb0 = nb * BN;
+        rb1 = nb * BN + 128;
+      }
+      const int g0 = rb0 >> 7, g1 = rb1 >> 7;
+      for (int ks = 0; ks < p.num_ks; ++ks) {
+        if (!mbar_wait(empty + stage, ph ^ 1, p.err, 0x101)) {
+          ok = false;
+          break;
+        }
+        uint32_t tx = A_BYTES + B_BYTES;
+        uint32_t sf_bytes = 0;
+        if (FP4) {
+          const int kb_here = min(4, p.kb_total - ks * 4);
+          sf_bytes = kb_here * 512;
+          tx += sf_bytes * (1 + (g0 < p.sfb_groups) + (g1 < p.sfb_groups));
+        }
+        mbar_expect_tx(full + stage, tx);
+        tma_load_2d(sA + stage * A_BYTES, &tmA, full + stage, ks * BKB, mb * BM);
+        tma_load_2d(sB + stage * B_BYTES, &tmB, full + stage, ks * BKB, rb0);
+        tma_load_2d(sB + stage * B_BYTES + 128 * BKB, &tmB, full + stage, ks * BKB, rb1);
+        if (FP4) {
+          const size_t chunk = (size_t)ks * 4;
+          bulk_load(sSFA + stage * SFA_BYTES, p.sfa + ((size_t)mb * p.sf_chunks + chunk) * 512, sf_bytes,
+                    full + stage);
+          if (g0 < p.sfb_groups)
+            bulk_load(sSFB + stage * SFB_BYTES, p.sfb + ((size_t)g0 * p.sf_chunks + chunk) * 512, sf_bytes,
+                      full + stage);
+          if (g1 < p.sfb_groups)
+            bulk_load(sSFB + stage * SFB_BYTES + 2048, p.sfb + ((size_t)g1 * p.sf_chunks + chunk) * 512, sf_bytes,
+                      full + stage);
+        }
+        issued |= 1u << stage;
+        last_ph = (last_ph & ~(1u << stage)) | (ph << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          ph ^= 1;
+        }
+      }
+    }
+    if (!ok) {  // let every copy already in flight land before the CTA exits
+      for (int s = 0; s < STAGES; ++s)
+        if (issued & (1u << s)) {
+          const uint32_t a = smem_u32(full + s);
+          const unsigned long long t0 = globaltimer();
+          while (!mbar_try(a, (last_ph >> s) & 1) && (long long)(globaltimer() - t0) < kWaitLimitNs) {
+          }
+        }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ----------------------------------------------------------------------------------------------- MMA
+    int stage = 0;
+    uint32_t ph = 0, acc_ph = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+      if (!mbar_wait(acc_empty, acc_ph ^ 1, p.err, 0x201)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      for (int ks = 0; ks < p.num_ks; ++ks) {
+        if (!mbar_wait(full + stage, ph, p.err, 0x202)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int kb_here = min(4, p.kb_total - ks * 4);
+        const uint32_t sfa_t = tmem + SF_COL + (stage & 1) * 48;
+        const uint32_t sfb_t = sfa_t + 16;
+        if (FP4) {
+          for (int kb = 0; kb < kb_here; ++kb) {
+            tc_cp_sf(sfa_t + kb * 4, desc_sf(sSFA + stage * SFA_BYTES + kb * 512));
+            tc_cp_sf(sfb_t + kb * 8, desc_sf(sSFB + stage * SFB_BYTES + kb * 512));
+            tc_cp_sf(sfb_t + kb * 8 + 4, desc_sf(sSFB + stage * SFB_BYTES + 2048 + kb * 512));
+          }
+        }
+        for (int kb = 0; kb < kb_here; ++kb) {
+          const uint64_t da = desc_sw128(sA + stage * A_BYTES + kb * 32);
+          const uint64_t db = desc_sw128(sB + stage * B_BYTES + kb * 32);
+          const uint32_t acc = (ks | kb) != 0;
+          if (FP4)
+            mma_fp4(tmem + ACC_COL, da, db, sfa_t + kb * 4, sfb_t + kb * 8, acc);
+          else
+            mma_fp8(tmem + ACC_COL, da, db, acc);
+        }
+        tc_commit(empty + stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          ph ^= 1;
+        }
+      }
+      if (!ok) break;
+      tc_commit(acc_full);
+      acc_ph ^= 1;
+    }
+    // drain: the commit arrives once every tcgen05 op this thread issued has completed
+    tc_commit(drain);
+    const uint32_t a = smem_u32(drain);
+    const unsigned long long t0 = globaltimer();
+    while (!mbar_try(a, 0) && (long long)(globaltimer() - t0) < kWaitLimitNs) {
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int r = q * 32 + lane;               // row inside the tile == TMEM lane
+    const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+    uint32_t acc_ph = 0;
+    const Nvfp4Enc enc = nvfp4_enc(MODE == MODE_FP4_SWIGLU ? p.h_g : 1.0f);
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      if (!mbar_wait(acc_full, acc_ph, p.err, 0x301)) break;
+      tc_fence_after();
+      const int mb = tile % p.num_m, nb = tile / p.num_m;
+      const int64_t m = (int64_t)mb * BM + r;
+      if (MODE == MODE_FP4_SWIGLU) {
+        const int F = p.N;
+        for (int c = 0; c < 4; ++c) {
+          float g[32], u[32];
+          tmem_ld32(trow + ACC_COL + c * 32, g);
+          tmem_ld32(trow + ACC_COL + 128 + c * 32, u);
+          if (c == 3) {
+            tc_fence_before();
+            mbar_arrive(acc_empty);
+          }
+          const int64_t col = (int64_t)nb * 128 + c * 32;  // hidden column of g[0]
+          if (m < p.M) {
+            float h[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float gv = bf16_round(g[j] * p.alpha), uv = bf16_round(u[j] * p.alpha);
+              g[j] = gv;
+              u[j] = uv;
+              h[j] = bf16_round(bf16_round(__fdiv_rn(gv, 1.0f + expf(-gv))) * uv);
+            }
+            if (p.gu_out) {
+              uint4* dg = reinterpret_cast<uint4*>(p.gu_out + m * 2 * F + col);
+              uint4* du = reinterpret_cast<uint4*>(p.gu_out + m * 2 * F + F + col);
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                dg[v] = make_uint4(pack_bf16x2(g[8 * v], g[8 * v + 1]), pack_bf16x2(g[8 * v + 2], g[8 * v + 3]),
+                                   pack_bf16x2(g[8 * v + 4], g[8 * v + 5]), pack_bf16x2(g[8 * v + 6], g[8 * v + 7]));
+                du[v] = make_uint4(pack_bf16x2(u[8 * v], u[8 * v + 1]), pack_bf16x2(u[8 * v + 2], u[8 * v + 3]),
+                                   pack_bf16x2(u[8 * v + 4], u[8 * v + 5]), pack_bf16x2(u[8 * v + 6], u[8 * v + 7]));
+              }
+            }
+            uint32_t sfv[2], cw[4];
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+              float amax = 0.0f;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(h[16 * blk + j]));
+              sfv[blk] = nvfp4_scale(amax, enc);
+              const float inv = nvfp4_inv(sfv[blk], enc);
+              cw[2 * blk] = nvfp4_codes8(h + 16 * blk, inv);
+              cw[2 * blk + 1] = nvfp4_codes8(h + 16 * blk + 8, inv);
+            }
+            *reinterpret_cast<uint4*>(p.h_codes + m * (F / 2) + col / 2) = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+            *reinterpret_cast<uint16_t*>(p.h_sf + sf_tiled_offset(m, col / 16, F / 64)) =
+                (uint16_t)(sfv[0] | (sfv[1] << 8));
+          } else {
+            *reinterpret_cast<uint16_t*>(p.h_sf + sf_tiled_offset(m, col / 16, F / 64)) = 0;
+          }
+        }
+      } else {
+        float scale = p.alpha;
+        if (MODE == MODE_FP8) scale = __ldg(p.a_scale) * (p.b_per_channel ? 1.0f : __ldg(p.b_scale));
+        for (int c = 0; c < 8; ++c) {
+          float v[32];
+          tmem_ld32(trow + ACC_COL + c * 32, v);
+          if (c == 7) {
+            tc_fence_before();
+            mbar_arrive(acc_empty);
+          }
+          const int64_t n0 = (int64_t)nb * BN + c * 32;
+          if (m < p.M && n0 < p.N) {
+            if (MODE == MODE_FP8 && p.b_per_channel) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] *= scale * __ldg(p.b_scale + n0 + j);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] *= scale;
+            }
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.y) + m * p.ldy + n0);
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+              dst[t] = make_uint4(pack_bf16x2(v[8 * t], v[8 * t + 1]), pack_bf16x2(v[8 * t + 2], v[8 * t + 3]),
+                                  pack_bf16x2(v[8 * t + 4], v[8 * t + 5]), pack_bf16x2(v[8 * t + 6], v[8 * t + 7]));
+          }
+        }
+      }
+      acc_ph ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+template <int MODE>
+tfb_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t s) {
+  const DeviceInfo* di;
+  tfb_status st = device_info(&di);
+  if (st != TFB_OK) return st;
+  static bool attr_set[64];
+  if (!attr_set[di->device]) {
+    TFB_CUDA(cudaFuncSetAttribute(gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(MODE)));
+    attr_set[di->device] = true;
+  }
+  const int grid = p.num_tiles < di->sm_count ? p.num_tiles : di->sm_count;
+  if (grid == 0) return TFB_OK;
+  gemm_kernel<MODE><<<grid, THREADS, smem_bytes(MODE), s>>>(ta, tb, p);
+  TFB_CUDA(cudaGetLastError());
+  return TFB_OK;
+}
+
+tfb_status check_common(int64_t M, int64_t N, int64_t K, const char* who) {
+  if (M < 0 || N <= 0 || K <= 0 || K % 128 || N % 32)
+    return fail(TFB_BAD_SHAPE, "%s: need K %% 128 == 0 and N %% 32 == 0 (M=%lld N=%lld K=%lld)", who, (long long)M,
+                (long long)N, (long long)K);
+  if (M > (int64_t)1 << 30 || N > (int64_t)1 << 30 || K > (int64_t)1 << 30)
+    return fail(TFB_BAD_SHAPE, "%s: dimension too large", who);
+  return TFB_OK;
+}
+
+void fill_tiles(Params& p, int64_t M, int64_t ncols_per_tile, int64_t N) {
+  p.num_m = (int)((M + BM - 1) / BM);
+  p.num_n = (int)((N + ncols_per_tile - 1) / ncols_per_tile);
+  p.num_tiles = p.num_m * p.num_n;
+}
+
+}  // namespace
+
+tfb_status gemm_nvfp4(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf, int64_t M,
+                      int64_t N, int64_t K, float alpha, void* y, int64_t ldy, cudaStream_t s) {
+  tfb_status st = check_common(M, N, K, "gemm_nvfp4");
+  if (st != TFB_OK) return st;
+  if (ldy < N || ldy % 8 || !aligned(y, 16) || !aligned(a_sf, 16) || !aligned(b_sf, 16))
+    return fail(TFB_BAD_ALIGN, "gemm_nvfp4: y/ldy need 16-byte alignment, scales 16-byte aligned");
+  const DeviceInfo* di;
+  if ((st = device_info(&di)) != TFB_OK) return st;
+  if (M == 0) return TFB_OK;
+  CUtensorMap ta, tb;
+  if ((st = make_tmap_u8(&ta, a, K / 2, M, K / 2, BKB, BM)) != TFB_OK) return st;
+  if ((st = make_tmap_u8(&tb, b, K / 2, N, K / 2, BKB, 128)) != TFB_OK) return st;
+  Params p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  fill_tiles(p, M, BN, N);
+  p.num_ks = (int)(K / 256 + (K % 256 ? 1 : 0));
+  p.kb_total = (int)(K / 64);
+  p.b_rows = (int)N;
+  p.sfa = a_sf;
+  p.sfb = b_sf;
+  p.sf_chunks = (int)(K / 64);
+  p.sfb_groups = (int)((N + 127) / 128);
+  p.y = y;
+  p.ldy = ldy;
+  p.alpha = alpha;
+  p.err = di->err_word;
+  return launch<MODE_FP4>(ta, tb, p, s);
+}
+
+tfb_status gemm_nvfp4_swiglu(const uint8_t* a, const uint8_t* a_sf, const uint8_t* gu, const uint8_t* gu_sf, int64_t M,
+                             int64_t F, int64_t K, float alpha, float h_g, uint8_t* h_codes, uint8_t* h_sf,
+                             void* gu_out, cudaStream_t s) {
+  tfb_status st = check_common(M, F, K, "gemm_nvfp4_swiglu");
+  if (st != TFB_OK) return st;
+  if (F % 128) return fail(TFB_BAD_SHAPE, "gemm_nvfp4_swiglu: F=%lld must be a multiple of 128", (long long)F);
+  if (!(h_g > 0.0f) || !isfinite(h_g)) return fail(TFB_BAD_ARG, "gemm_nvfp4_swiglu: h_global must be positive");
+  if (!aligned(h_codes, 16) || !aligned(h_sf, 16) || !aligned(a_sf, 16) || !aligned(gu_sf, 16) ||
+      (gu_out && !aligned(gu_out, 16)))
+    return fail(TFB_BAD_ALIGN, "gemm_nvfp4_swiglu: outputs and scales must be 16-byte aligned");
+  const DeviceInfo* di;
+  if ((st = device_info(&di)) != TFB_OK) return st;
+  if (M == 0) return TFB_OK;
+  CUtensorMap ta, tb;
+  if ((st = make_tmap_u8(&ta, a, K / 2, M, K / 2, BKB, BM)) != TFB_OK) return st;
+  if ((st = make_tmap_u8(&tb, gu, K / 2, 2 * F, K / 2, BKB, 128)) != TFB_OK) return st;
+  Params p{};
+  p.M = (int)M;
+  p.N = (int)F;
+  fill_tiles(p, M, 128, F);
+  p.num_ks = (int)(K / 256 + (K % 256 ? 1 : 0));
+  p.kb_total = (int)(K / 64);
+  p.b_rows = (int)(2 * F);
+  p.sfa = a_sf;
+  p.sfb = gu_sf;
+  p.sf_chunks = (int)(K / 64);
+  p.sfb_groups = (int)((2 * F + 127) / 128);
+  p.alpha = alpha;
+  p.h_g = h_g;
+  p.h_codes = h_codes;
+  p.h_sf = h_sf;
+  p.gu_out = static_cast<__nv_bfloat16*>(gu_out);
+  p.err = di->err_word;
+  return launch<MODE_FP4_SWIGLU>(ta, tb, p, s);
+}
+
+tfb_status gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, int64_t K, const float* a_scale,
+                    const float* b_scale, int per_channel, void* y, int64_t ldy, cudaStream_t s) {
+  tfb_status st = check_common(M, N, K, "gemm_fp8");
+  if (st != TFB_OK) return st;
+  if (ldy < N || ldy % 8 || !aligned(y, 16) || !aligned(a_scale, 4) || !aligned(b_scale, 4))
+    return fail(TFB_BAD_ALIGN, "gemm_fp8: y/ldy need 16-byte alignment");
+  const DeviceInfo* di;
+  if ((st = device_info(&di)) != TFB_OK) return st;
+  if (M == 0) return TFB_OK;
+  CUtensorMap ta, tb;
+  if ((st = make_tmap_u8(&ta, a, K, M, K, BKB, BM)) != TFB_OK) return st;
+  if ((st = make_tmap_u8(&tb, b, K, N, K, BKB, 128)) != TFB_OK) return st;
+  Params p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  fill_tiles(p, M, BN, N);
+  p.num_ks = (int)(K / 128);
+  p.kb_total = (int)(K / 32);
+  p.b_rows = (int)N;
+  p.y = y;
+  p.ldy = ldy;
+  p.a_scale = a_scale;
+  p.b_scale = b_scale;
+  p.b_per_channel = per_channel;
+  p.err = di->err_word;
+  return launch<MODE_FP8>(ta, tb, p, s);
+}
+
+}  // namespace tfb
+
+extern "C" {
+
+tfb_status tfb_gemm_nvfp4(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* b_codes, const uint8_t* b_sf,
+                          int64_t M, int64_t N, int64_t K, float alpha, void* y, int64_t ldy, void* stream) {
+  return tfb::gemm_nvfp4(a_codes, a_sf, b_codes, b_sf, M, N, K, alpha, y, ldy, static_cast<cudaStream_t>(stream));
+}
+
+tfb_status tfb_gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, int64_t K, const float* a_scale,
+                        const float* b_scale, int b_per_channel, void* y, int64_t ldy, void* stream) {
+  return tfb::gemm_fp8(a, b, M, N, K, a_scale, b_scale, b_per_channel, y, ldy, static_cast<cudaStream_t>(stream));
+}
+
+tfb_status tfb_gemm_nvfp4_swiglu(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* gu_codes,
+                                 const uint8_t* gu_sf, int64_t M, int64_t F, int64_t K, float alpha, float h_global,
+                                 uint8_t* h_codes, uint8_t* h_sf, void* gu_out, void* stream) {
+  return tfb::gemm_nvfp4_swiglu(a_codes, a_sf, gu_codes, gu_sf, M, F, K, alpha, h_global, h_codes, h_sf, gu_out,
+                                static_cast<cudaStream_t>(stream));
+}
+
+tfb_status tfb_mlp_nvfp4(const void* x, int64_t M, int64_t K, int64_t F, float act_x, const uint8_t* gu_codes,
+                         const uint8_t* gu_sf, float g_gu, const uint8_t* down_codes, const uint8_t* down_sf,
+                         float g_down, float act_h, void* y, uint8_t* ws_xc, uint8_t* ws_xsf, uint8_t* ws_hc,
+                         uint8_t* ws_hsf, void* stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  tfb_status st = tfb::quant_nvfp4(x, M, K, K, act_x, ws_xc, ws_xsf, TFB_SF_TILED, s);
+  if (st != TFB_OK) return st;
+  st = tfb::gemm_nvfp4_swiglu(ws_xc, ws_xsf, gu_codes, gu_sf, M, F, K, (float)((double)act_x * g_gu), act_h, ws_hc,
+                              ws_hsf, nullptr, s);
+  if (st != TFB_OK) return st;
+  return tfb::gemm_nvfp4(ws_hc, ws_hsf, down_codes, down_sf, M, K, F, (float)((double)act_h * g_down), y, K, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,118 @@
+// Host plumbing of libtfb: error reporting, per-device cache, TMA tensor maps, small C entry points.
+#include <cudaTypedefs.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "tfb_common.cuh"
+
+namespace tfb {
+
+// Kernels whose bounded waits run out record a nonzero code here (one word per device context).
+__device__ int g_err_word;
+
+static thread_local char t_msg[512];
+
+tfb_status fail(tfb_status st, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_msg, sizeof(t_msg), fmt, ap);
+  va_end(ap);
+  return st;
+}
+
+tfb_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(TFB_CUDA_ERR, "%s failed: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+namespace {
+constexpr int kMaxDevices = 64;
+DeviceInfo g_dev[kMaxDevices];
+bool g_dev_ok[kMaxDevices];
+std::mutex g_dev_mu;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+}  // namespace
+
+tfb_status device_info(const DeviceInfo** out) {
+  int dev = 0;
+  TFB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(TFB_BAD_ARG, "device ordinal %d out of range", dev);
+  if (g_dev_ok[dev]) {
+    *out = &g_dev[dev];
+    return TFB_OK;
+  }
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  if (!g_dev_ok[dev]) {
+    int major = 0, minor = 0, sms = 0;
+    TFB_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    TFB_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+    TFB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    if (major != 10 || minor != 0)
+      return fail(TFB_BAD_ARCH, "libtfb is built for sm_100a (B200); device %d is sm_%d%d", dev, major, minor);
+    void* p = nullptr;
+    TFB_CUDA(cudaGetSymbolAddress(&p, g_err_word));
+    g_dev[dev] = DeviceInfo{dev, sms, static_cast<int*>(p)};
+    g_dev_ok[dev] = true;
+  }
+  *out = &g_dev[dev];
+  return TFB_OK;
+}
+
+tfb_status make_tmap_u8(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint64_t row_stride,
+                        uint32_t box_inner, uint32_t box_rows) {
+  if (!g_encode) {
+    std::lock_guard<std::mutex> lock(g_dev_mu);
+    if (!g_encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      TFB_CUDA(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q));
+      if (q != cudaDriverEntryPointSuccess || !fn) return fail(TFB_CUDA_ERR, "cuTensorMapEncodeTiled unavailable");
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  }
+  if (!aligned(base, 16) || row_stride % 16 != 0)
+    return fail(TFB_BAD_ALIGN, "TMA operand needs a 16-byte aligned base and row stride (stride %llu)",
+                (unsigned long long)row_stride);
+  cuuint64_t dims[2] = {inner_bytes, rows};
+  cuuint64_t strides[1] = {row_stride};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TFB_CUDA_ERR, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+  return TFB_OK;
+}
+
+}  // namespace tfb
+
+extern "C" {
+
+int tfb_version(void) { return 100; }
+
+const char* tfb_last_error(void) { return tfb::t_msg; }
+
+int64_t tfb_sf_tiled_bytes(int64_t rows, int64_t k) {
+  if (rows < 0 || k < 0 || k % 64) return -1;
+  return ((rows + 127) / 128) * (k / 64) * 512;
+}
+
+tfb_status tfb_device_status(int* code, int reset) {
+  const tfb::DeviceInfo* di;
+  tfb_status st = tfb::device_info(&di);
+  if (st != TFB_OK) return st;
+  TFB_CUDA(cudaDeviceSynchronize());
+  int v = 0;
+  TFB_CUDA(cudaMemcpy(&v, di->err_word, sizeof(int), cudaMemcpyDeviceToHost));
+  if (reset && v) {
+    int z = 0;
+    TFB_CUDA(cudaMemcpy(di->err_word, &z, sizeof(int), cudaMemcpyHostToDevice));
+  }
+  if (code) *code = v;
+  if (v) return tfb::fail(TFB_DEVICE_TIMEOUT, "a kernel pipeline wait ran out (code 0x%x)", v);
+  return TFB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,225 @@
+"""ctypes binding of libtfb.so (the C ABI in ``include/tfb.h``) plus thin torch-tensor wrappers.
+
+Every wrapper validates nothing beyond what it needs to build pointers: the library checks shapes, alignment and
+the device architecture itself and returns a status, which :func:`check` turns into ``TfbError`` (a
+``RuntimeError``) carrying ``tfb_last_error()``. Work goes on torch's current CUDA stream; nothing here syncs
+except :func:`device_status`. There is no fallback: if the library cannot be loaded, every op raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+LIB_NAME = "libtfb.so"
+DEFAULT_DIR = Path(__file__).resolve().parent
+
+c_i64, c_int, c_float, c_vp = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_void_p
+
+# name -> argtypes, mirroring include/tfb.h
+SIGNATURES = {
+    "tfb_version": [],
+    "tfb_last_error": [],
+    "tfb_sf_tiled_bytes": [c_i64, c_i64],
+    "tfb_device_status": [ctypes.POINTER(c_int), c_int],
+    "tfb_absmax_bf16": [c_vp, c_i64, c_vp, c_vp],
+    "tfb_fp8_act_scale": [c_vp, c_i64, c_vp, c_vp],
+    "tfb_quant_nvfp4": [c_vp, c_i64, c_i64, c_i64, c_float, c_vp, c_vp, c_int, c_vp],
+    "tfb_quant_fp8": [c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp],
+    "tfb_gemm_nvfp4": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_vp, c_i64, c_vp],
+    "tfb_gemm_fp8": [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_int, c_vp, c_i64, c_vp],
+    "tfb_gemm_nvfp4_swiglu": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_float, c_vp, c_vp, c_vp, c_vp],
+    "tfb_mlp_nvfp4": [c_vp, c_i64, c_i64, c_i64, c_float, c_vp, c_vp, c_float, c_vp, c_vp, c_float, c_float, c_vp,
+                      c_vp, c_vp, c_vp, c_vp, c_vp],
+    "tfb_adaln": [c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_float, c_vp, c_float, c_vp, c_vp, c_vp],
+    "tfb_rms_rope": [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_float, c_vp, c_i64,
+                     c_i64, c_vp],
+    "tfb_swiglu": [c_vp, c_i64, c_i64, c_vp, c_vp],
+}
+RESTYPES = {"tfb_version": c_int, "tfb_last_error": ctypes.c_char_p, "tfb_sf_tiled_bytes": c_i64}
+
+SF_ROWS, SF_TILED = 0, 1
+STATUS = {0: "OK", 1: "BAD_SHAPE", 2: "BAD_ALIGN", 3: "BAD_ARCH", 4: "DEVICE_TIMEOUT", 5: "CUDA_ERR", 6: "BAD_ARG"}
+
+_lib = None
+_path: Path | None = None
+
+
+class TfbError(RuntimeError):
+    """A libtfb entry point returned a non-OK status."""
+
+
+def lib_path(directory: str | os.PathLike | None = None) -> Path:
+    root = Path(directory or os.environ.get("TFIMAGE_EXT_DIR") or DEFAULT_DIR)
+    return root / LIB_NAME
+
+
+def load(directory: str | os.PathLike | None = None):
+    """Load libtfb.so once (from ``directory``, ``$TFIMAGE_EXT_DIR`` or this package) and bind its symbols."""
+    global _lib, _path
+    if _lib is not None and (directory is None or lib_path(directory) == _path):
+        return _lib
+    path = lib_path(directory)
+    if not path.is_file():
+        raise TfbError(f"{path} not found: build it with qwen-image21-tensorfold-rtx_b200/build.py "
+                       f"(there is no fallback path)")
+    lib = ctypes.CDLL(str(path))
+    for name, args in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = RESTYPES.get(name, c_int)
+    _lib, _path = lib, path
+    return lib
+
+
+def check(status: int) -> None:
+    if status != 0:
+        msg = load().tfb_last_error().decode(errors="replace")
+        raise TfbError(f"libtfb {STATUS.get(status, status)}: {msg}")
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise TfbError("libtfb ops take CUDA tensors (there is no CPU path)")
+
+
+def sf_tiled_bytes(rows: int, k: int) -> int:
+    return int(load().tfb_sf_tiled_bytes(rows, k))
+
+
+def device_status(reset: bool = True) -> int:
+    code = c_int(0)
+    st = load().tfb_device_status(ctypes.byref(code), int(reset))
+    if st not in (0, 4):
+        check(st)
+    return code.value
+
+
+# ----------------------------------------------------------------------------------------------- tensor wrappers
+def absmax(x: torch.Tensor) -> torch.Tensor:
+    """Device fp32 scalar amax(|x|) of a bf16 tensor (contiguous)."""
+    _cuda(x)
+    x = x.contiguous()
+    out = torch.empty((), dtype=torch.float32, device=x.device)
+    check(load().tfb_absmax_bf16(x.data_ptr(), x.numel(), out.data_ptr(), _stream(x)))
+    return out
+
+
+def fp8_act_scale(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    _cuda(x)
+    x = x.contiguous()
+    out = torch.empty((), dtype=torch.float32, device=x.device) if out is None else out
+    check(load().tfb_fp8_act_scale(x.data_ptr(), x.numel(), out.data_ptr(), _stream(x)))
+    return out
+
+
+def quant_nvfp4(x: torch.Tensor, g: float, layout: int = SF_TILED, codes=None, sf=None):
+    """bf16 [M, K] -> (codes uint8 [M, K/2], scales uint8: [M, K/16] rows or tiled bytes)."""
+    _cuda(x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise TfbError("quant_nvfp4 takes a 2-D bf16 tensor with unit column stride")
+    M, K = x.shape
+    if codes is None:
+        codes = torch.empty((M, K // 2), dtype=torch.uint8, device=x.device)
+    if sf is None:
+        sf = (torch.empty((max(sf_tiled_bytes(M, K), 0),), dtype=torch.uint8, device=x.device) if layout == SF_TILED
+              else torch.empty((M, K // 16), dtype=torch.uint8, device=x.device))
+    check(load().tfb_quant_nvfp4(x.data_ptr(), M, K, x.stride(0), float(g), codes.data_ptr(), sf.data_ptr(), layout,
+                                 _stream(x)))
+    return codes, sf
+
+
+def quant_fp8(x: torch.Tensor, a: torch.Tensor, out=None) -> torch.Tensor:
+    _cuda(x, a)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise TfbError("quant_fp8 takes a 2-D bf16 tensor with unit column stride")
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.uint8, device=x.device) if out is None else out
+    check(load().tfb_quant_fp8(x.data_ptr(), M, K, x.stride(0), a.data_ptr(), q.data_ptr(), _stream(x)))
+    return q
+
+
+def gemm_nvfp4(a_codes, a_sf, b_codes, b_sf, M: int, N: int, K: int, alpha: float, out=None) -> torch.Tensor:
+    _cuda(a_codes, a_sf, b_codes, b_sf)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=a_codes.device) if out is None else out
+    check(load().tfb_gemm_nvfp4(a_codes.data_ptr(), a_sf.data_ptr(), b_codes.data_ptr(), b_sf.data_ptr(), M, N, K,
+                                float(alpha), y.data_ptr(), y.stride(0), _stream(a_codes)))
+    return y
+
+
+def gemm_fp8(a8, b8, M: int, N: int, K: int, a_scale, b_scale, out=None) -> torch.Tensor:
+    _cuda(a8, b8, a_scale, b_scale)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=a8.device) if out is None else out
+    per_channel = int(b_scale.numel() > 1)
+    check(load().tfb_gemm_fp8(a8.data_ptr(), b8.data_ptr(), M, N, K, a_scale.data_ptr(), b_scale.data_ptr(),
+                              per_channel, y.data_ptr(), y.stride(0), _stream(a8)))
+    return y
+
+
+def gemm_nvfp4_swiglu(a_codes, a_sf, gu_codes, gu_sf, M: int, F: int, K: int, alpha: float, h_global: float,
+                      h_codes=None, h_sf=None, gu_out=None):
+    _cuda(a_codes, a_sf, gu_codes, gu_sf)
+    dev = a_codes.device
+    if h_codes is None:
+        h_codes = torch.empty((M, F // 2), dtype=torch.uint8, device=dev)
+    if h_sf is None:
+        h_sf = torch.empty((sf_tiled_bytes(M, F),), dtype=torch.uint8, device=dev)
+    check(load().tfb_gemm_nvfp4_swiglu(a_codes.data_ptr(), a_sf.data_ptr(), gu_codes.data_ptr(), gu_sf.data_ptr(), M, F,
+                                       K, float(alpha), float(h_global), h_codes.data_ptr(), h_sf.data_ptr(),
+                                       _ptr(gu_out), _stream(a_codes)))
+    return h_codes, h_sf
+
+
+def mlp_nvfp4(x, F: int, act_x: float, gu_codes, gu_sf, g_gu: float, down_codes, down_sf, g_down: float,
+              act_h: float, out=None, workspace=None) -> torch.Tensor:
+    _cuda(x, gu_codes, gu_sf, down_codes, down_sf)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or not x.is_contiguous():
+        raise TfbError("mlp_nvfp4 takes a contiguous 2-D bf16 tensor")
+    M, K = x.shape
+    dev = x.device
+    y = torch.empty((M, K), dtype=torch.bfloat16, device=dev) if out is None else out
+    ws = workspace or mlp_workspace(M, K, F, dev)
+    check(load().tfb_mlp_nvfp4(x.data_ptr(), M, K, F, float(act_x), gu_codes.data_ptr(), gu_sf.data_ptr(), float(g_gu),
+                               down_codes.data_ptr(), down_sf.data_ptr(), float(g_down), float(act_h), y.data_ptr(),
+                               ws[0].data_ptr(), ws[1].data_ptr(), ws[2].data_ptr(), ws[3].data_ptr(), _stream(x)))
+    return y
+
+
+def mlp_workspace(M: int, K: int, F: int, device) -> tuple[torch.Tensor, ...]:
+    """Caller-owned scratch of tfb_mlp_nvfp4: x codes/scales and hidden codes/scales."""
+    u8 = dict(dtype=torch.uint8, device=device)
+    return (torch.empty((M, K // 2), **u8), torch.empty((sf_tiled_bytes(M, K),), **u8),
+            torch.empty((M, F // 2), **u8), torch.empty((sf_tiled_bytes(M, F),), **u8))
+
+
+def adaln(x, scale, shift, eps: float, out=None, q_global: float | None = None, codes=None, sf=None):
+    _cuda(x, scale, shift)
+    B, N, D = x.shape
+    check(load().tfb_adaln(x.data_ptr(), B, N, D, scale.data_ptr(), _ptr(shift), float(eps), _ptr(out),
+                           float(q_global or 0.0), _ptr(codes), _ptr(sf), _stream(x)))
+
+
+def rms_rope(src, part: int, w, cos, sin, eps: float, dst) -> None:
+    _cuda(src, w, cos, sin, dst)
+    B, N, _, H, D = src.shape
+    check(load().tfb_rms_rope(src.data_ptr(), B, N, H, D, src.stride(0), src.stride(1), part * H * D, w.data_ptr(),
+                              cos.data_ptr(), sin.data_ptr(), float(eps), dst.data_ptr(), dst.stride(0),
+                              dst.stride(1), _stream(src)))
+
+
+def swiglu(gu, out) -> None:
+    _cuda(gu, out)
+    M, F2 = gu.shape
+    check(load().tfb_swiglu(gu.data_ptr(), M, F2 // 2, out.data_ptr(), _stream(gu)))

@@ -1,0 +1,249 @@
+"""Linear layers for DiT steps on B200: bf16 (reference), FP8 W8A8 and NVFP4 W4A4 on libtfb's tcgen05 GEMMs.
+
+Drop-in for the reference ``tfimage/linear.py`` (same names, arguments and semantics; reference lines cited per
+symbol). Activations are quantized under a per-layer input scale ``act``: measured on the fly (``act=None``: the
+NVFP4 path reads amax back to the host once per call, exactly like the reference, because calibration consumes
+it as a Python float) or fixed from a calibration run (no host sync, CUDA-graph safe). Per-16 NVFP4 block scales
+still follow every row's range.
+
+Differences from the reference, all forced by the hardware or by the absent TensorFold library:
+  * ``nvfp4_supported`` gates on compute capability 10.0 and on libtfb loading (the reference gates on 12.x);
+  * the ``Fp4Linear`` container keeps the reference attribute names but its own layout: ``words`` are the NVFP4
+    codes viewed as int32 [N, K/8], ``bs`` the scale bytes in the GEMM's tiled layout;
+  * NVFP4 needs ``k % 128 == 0 and n % 64 == 0`` (as in the reference); the FP8 GEMM needs ``k % 128 == 0 and
+    n % 32 == 0`` (the reference's cuBLASLt path took ``% 16``), other shapes go to bf16 as before;
+  * ``Fp8Linear`` optionally takes per-output-channel weight scales (``per_channel=True``).
+"""
+
+from __future__ import annotations
+
+from functools import lru_cache
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+
+FP4_MAX, E4M3_MAX = 6.0, 448.0
+# Tile ids the reference passed to TensorFold's prompt GEMM (linear.py:17). They are accepted for API and
+# engine-file compatibility; the sm_100a library has one persistent 128x256 tcgen05 tile, used for all of them.
+TILES = (0, 1, 2, 12, 13)
+
+
+@lru_cache(maxsize=1)
+def nvfp4_supported() -> bool:
+    """linear.py:25-27, for B200: a CUDA device of compute capability 10.0 and a loadable libtfb."""
+    if not torch.cuda.is_available() or torch.cuda.get_device_capability() != (10, 0):
+        return False
+    try:
+        _lib.load()
+    except OSError:
+        return False
+    return True
+
+
+def nvfp4_weight(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, float]:
+    """linear.py:30-38: bf16 [N, K] -> (e2m1 codes [N, K/2] uint8, e4m3 scales [N, K/16], global scale)."""
+    n, k = w.shape
+    g = max(float(w.float().abs().amax()), 1e-12) / (FP4_MAX * E4M3_MAX)
+    wb = w.to(torch.bfloat16).contiguous()
+    codes, scales = _lib.quant_nvfp4(wb, g, _lib.SF_ROWS)
+    return codes, scales.view(torch.float8_e4m3fn), g
+
+
+# ------------------------------------------------------------------------------------------ scale-layout helpers
+def sf_tile(rows: torch.Tensor) -> torch.Tensor:
+    """Row-major scale bytes [R, K/16] -> the GEMM's tiled layout [ceil(R/128) * K/64 * 512] (zero-padded rows)."""
+    rows = rows.view(torch.uint8)
+    R, S = rows.shape
+    Rp = (R + 127) // 128 * 128
+    if Rp != R:
+        rows = torch.cat([rows, rows.new_zeros((Rp - R, S))])
+    return rows.reshape(Rp // 128, 4, 32, S // 4, 4).permute(0, 3, 2, 1, 4).reshape(-1).contiguous()
+
+
+def sf_untile(tiled: torch.Tensor, R: int, K: int) -> torch.Tensor:
+    S = K // 16
+    Rp = (R + 127) // 128 * 128
+    return tiled.view(torch.uint8).reshape(Rp // 128, S // 4, 32, 4, 4).permute(0, 3, 2, 1, 4).reshape(Rp, S)[:R]
+
+
+class Fp4Linear:
+    """NVFP4 weight container with the attribute names tfimage's engine store uses (store.py:38-42,66-71).
+
+    ``words``: codes as int32 [N, K/8] (8 E2M1 values per word, even element in the lowest nibble);
+    ``bs``: scale bytes, tiled for the GEMM; ``scale``: weight global g; ``act``: input global."""
+
+    def __init__(self, words: torch.Tensor, bs: torch.Tensor, scale: float, n: int, k: int, act: float = 1.0):
+        self.words, self.bs, self.scale, self.n, self.k, self.act = words, bs, float(scale), int(n), int(k), float(act)
+
+    @classmethod
+    def from_checkpoint(cls, codes: torch.Tensor, scales: torch.Tensor, g: float, act: float = 1.0) -> "Fp4Linear":
+        n, half_k = codes.shape
+        words = codes.contiguous().view(torch.int32)
+        return cls(words, sf_tile(scales.contiguous()), g, n, half_k * 2, act)
+
+    @property
+    def codes(self) -> torch.Tensor:
+        return self.words.view(torch.uint8)
+
+    def scales(self) -> torch.Tensor:
+        """Row-major e4m3 scales [N, K/16] (the nvfp4_weight view)."""
+        return sf_untile(self.bs, self.n, self.k).view(torch.float8_e4m3fn)
+
+    def tiles(self, a: int, b: int) -> "Fp4Linear":
+        """Rows [64a, 64b) as their own container (the reference's N-tiles of 64 rows)."""
+        codes = self.codes[64 * a:64 * b]
+        scales = self.scales()[64 * a:64 * b]
+        return Fp4Linear.from_checkpoint(codes, scales, self.scale, self.act)
+
+
+class Nvfp4Act:
+    """Activations already quantized under ``act`` (e.g. by the AdaLN fusion): codes [M, K/2] + tiled scales."""
+
+    def __init__(self, codes: torch.Tensor, sf: torch.Tensor, act: float, m: int, k: int):
+        self.codes, self.sf, self.act, self.m, self.k = codes, sf, float(act), int(m), int(k)
+
+
+class Linear:
+    """y = x @ W^T for 2-D bf16 rows; ``kind`` names the backend (linear.py:41-52)."""
+
+    kind = "base"
+    n: int
+    k: int
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        raise NotImplementedError
+
+    def nbytes(self) -> int:
+        raise NotImplementedError
+
+
+class Bf16Linear(Linear):
+    """linear.py:55-67 (cuBLAS through F.linear; not a hot-path kernel)."""
+
+    kind = "bf16"
+
+    def __init__(self, w: torch.Tensor):
+        self.w = w.to(torch.bfloat16).contiguous()
+        self.n, self.k = self.w.shape
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        w = self.w if self.w.device == x.device else self.w.to(x.device, non_blocking=True)
+        return F.linear(x, w)
+
+    def nbytes(self) -> int:
+        return self.w.numel() * 2
+
+
+class Fp8Linear(Linear):
+    """linear.py:70-102: W8A8 e4m3 with one input scale (static or measured on the device) and a tensor-wise --
+    or, with ``per_channel=True``, per-output-channel -- weight scale, on libtfb's tcgen05 FP8 GEMM."""
+
+    kind = "fp8"
+
+    def __init__(self, w: torch.Tensor, act: float | None = None, per_channel: bool = False):
+        w = w.float()
+        self.n, self.k = w.shape
+        if per_channel:
+            s = (w.abs().amax(dim=1) / E4M3_MAX).clamp_min(1e-12)
+            self.w8 = (w / s[:, None]).to(torch.float8_e4m3fn).contiguous()
+            self.ws = s.contiguous()
+        else:
+            s = (w.abs().amax() / E4M3_MAX).clamp_min(1e-12)
+            self.w8 = (w / s).to(torch.float8_e4m3fn).contiguous()
+            self.ws = s.view(()).contiguous()
+        self.act = act
+        self._a = None
+        self._a_val = None
+
+    def _act(self, x: torch.Tensor) -> torch.Tensor:
+        if self.act is None:
+            return _lib.fp8_act_scale(x)
+        if self._a is None or self._a.device != x.device or self._a_val != self.act:
+            self._a = torch.tensor(self.act, dtype=torch.float32, device=x.device)
+            self._a_val = self.act
+        return self._a
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        x = x.to(torch.bfloat16)
+        if x.stride(-1) != 1:
+            x = x.contiguous()
+        a = self._act(x)
+        w8, ws = self.w8, self.ws
+        if w8.device != x.device:
+            self.w8, self.ws = w8, ws = w8.to(x.device), ws.to(x.device)
+        q = _lib.quant_fp8(x, a)
+        return _lib.gemm_fp8(q, w8.view(torch.uint8), x.shape[0], self.n, self.k, a, ws)
+
+    def nbytes(self) -> int:
+        return self.w8.numel() + 4 * self.ws.numel()
+
+
+class Nvfp4Linear(Linear):
+    """linear.py:105-133: W4A4 NVFP4 (e2m1 values, e4m3 scale per 16, fp32 global) on libtfb's block-scaled
+    tcgen05 GEMM. ``tile`` is kept for API compatibility (see ``TILES``)."""
+
+    kind = "nvfp4"
+
+    def __init__(self, w: torch.Tensor, act: float | None = None, tile: int = 12):
+        codes, scales, g = nvfp4_weight(w)
+        self.lin = Fp4Linear.from_checkpoint(codes, scales, g, act=act if act is not None else 1.0)
+        self.n, self.k = self.lin.n, self.lin.k
+        self.dynamic = act is None
+        self.tile = tile
+        self.amax = 0.0                 # largest input scale seen (calibration)
+
+    def set_act(self, act: float | None) -> None:
+        self.dynamic = act is None
+        if act is not None:
+            self.lin.act = float(act)
+
+    def quantize(self, x: torch.Tensor) -> Nvfp4Act:
+        """Quantize rows under this layer's input scale (measuring it first in dynamic mode, linear.py:126-129)."""
+        if self.dynamic:
+            a = max(float(_lib.absmax(x)), 1e-6) / (FP4_MAX * E4M3_MAX)
+            self.amax = max(self.amax, a)
+            self.lin.act = a
+        if x.dtype != torch.bfloat16 or x.stride(-1) != 1:
+            x = x.to(torch.bfloat16).contiguous()
+        codes, sf = _lib.quant_nvfp4(x, self.lin.act, _lib.SF_TILED)
+        return Nvfp4Act(codes, sf, self.lin.act, x.shape[0], self.k)
+
+    def __call__(self, x) -> torch.Tensor:
+        q = x if isinstance(x, Nvfp4Act) else self.quantize(x)
+        lin = self.lin
+        return _lib.gemm_nvfp4(q.codes, q.sf, lin.codes, lin.bs, q.m, lin.n, lin.k, q.act * lin.scale)
+
+    def nbytes(self) -> int:
+        return self.lin.words.numel() * 4 + self.lin.bs.numel()
+
+
+def swiglu_mlp(gate_up: Linear, down: Linear, x: torch.Tensor):
+    """linear.py:136-150: down(silu(gate) * up) in one pass when both are static-scale NVFP4: the gate/up GEMM's
+    epilogue writes the SwiGLU rows as NVFP4 under down's input scale, so no bf16 [M, 2F] or [M, F] tensor exists.
+    None if the layers cannot take it (the caller runs the unfused path). Needs F % 128 == 0 here (the reference:
+    F % 64)."""
+
+    if not (isinstance(gate_up, Nvfp4Linear) and isinstance(down, Nvfp4Linear)) or gate_up.dynamic or down.dynamic:
+        return None
+    f = gate_up.n // 2
+    if f % 128 or down.k != f:
+        return None
+    q = x if isinstance(x, Nvfp4Act) else gate_up.quantize(x)
+    gu = gate_up.lin
+    h_codes, h_sf = _lib.gemm_nvfp4_swiglu(q.codes, q.sf, gu.codes, gu.bs, q.m, f, gu.k, q.act * gu.scale,
+                                           down.lin.act)
+    return _lib.gemm_nvfp4(h_codes, h_sf, down.lin.codes, down.lin.bs, q.m, down.n, f, down.lin.act * down.lin.scale)
+
+
+def make(kind: str, w: torch.Tensor, act: float | None = None) -> Linear:
+    """linear.py:153-161: a backend by name for a bf16 [N, K] weight (dims the kernels cannot tile fall back to
+    FP8, then bf16, as in the reference)."""
+
+    n, k = w.shape
+    if kind == "nvfp4" and nvfp4_supported() and k % 128 == 0 and n % 64 == 0:
+        return Nvfp4Linear(w, act)
+    if kind in ("nvfp4", "fp8") and k % 128 == 0 and n % 32 == 0:
+        return Fp8Linear(w, act)
+    return Bf16Linear(w)

@@ -1,0 +1,148 @@
+"""tcgen05 GEMMs against the oracle's dequantize-then-fp32-matmul (rel-L2 <= 2e-3 NVFP4, <= 1e-3 FP8)."""
+
+import numpy as np
+import pytest
+import torch
+from _helpers import bf16_cpu, f32, quant_weight, rel_l2, u8
+
+from oracle import fp8 as ofp8
+from oracle import fusions as ofu
+from oracle import nvfp4 as onv
+from tfimage import _lib
+from tfimage import linear as L
+
+pytestmark = pytest.mark.gpu
+TOL_NVFP4 = 2e-3   # GEMM outputs within rel-L2 2e-3 of dequant -> fp32 matmul
+TOL_FP8 = 1e-3
+
+
+def nvfp4_case(dev, M, N, K, seed):
+    x = bf16_cpu((M, K), seed=seed, outliers=8)
+    w = bf16_cpu((N, K), seed=seed + 1, scale=0.02)
+    wc, ws, gw = quant_weight(w)
+    ga = onv.dynamic_act_global(float(x.float().abs().max()))
+    xc, xs = onv.quantize(x.float().numpy(), ga)
+    ref = onv.bf16_round(onv.gemm(xc, xs, ga, wc, ws, gw))
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)   # noqa: E731
+    y = _lib.gemm_nvfp4(t(xc), t(onv.sf_tile(xs)), t(wc), t(onv.sf_tile(ws)), M, N, K, ga * gw)
+    return f32(y), ref
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 256), (1, 32, 128), (300, 320, 384), (1000, 1024, 640)])
+def test_gemm_nvfp4_shapes(dev, M, N, K):
+    y, ref = nvfp4_case(dev, M, N, K, seed=M + N + K)
+    assert rel_l2(y, ref) <= TOL_NVFP4
+    assert np.isfinite(y).all()
+
+
+def test_gemm_nvfp4_config0(dev):
+    """X [4096, 3072] (8 outlier channels x20) x W [3072, 3072] N(0, 0.02)."""
+    y, ref = nvfp4_case(dev, 4096, 3072, 3072, seed=0)
+    assert rel_l2(y, ref) <= TOL_NVFP4
+    assert (y == ref).mean() > 0.9            # most outputs round to the same bf16
+
+
+def test_gemm_nvfp4_repeatable(dev):
+    y1, _ = nvfp4_case(dev, 512, 512, 512, seed=3)
+    y2, _ = nvfp4_case(dev, 512, 512, 512, seed=3)
+    np.testing.assert_array_equal(y1, y2)
+
+
+@pytest.mark.parametrize("M,per_channel", [(4968, False), (4968, True), (77, True)])
+def test_gemm_fp8_config3(dev, M, per_channel):
+    """ragged M = 4712 + 256 = 4968, K = N = 3072; per-tensor act, tensor-wise or per-channel W."""
+    K = N = 3072 if M > 100 else 256
+    x = bf16_cpu((M, K), seed=M, outliers=8)
+    w = bf16_cpu((N, K), seed=M + 1, scale=0.02)
+    w8, ws = ofp8.weight(w.float().numpy(), per_channel)
+    xd = x.to(dev)
+    a = _lib.fp8_act_scale(xd)
+    q = _lib.quant_fp8(xd, a)
+    y = _lib.gemm_fp8(q, torch.from_numpy(w8).to(dev), M, N, K, a, torch.from_numpy(np.atleast_1d(ws)).to(dev))
+    ref = ofp8.gemm(u8(q), float(a), w8, ws)
+    assert rel_l2(f32(y), ref) <= TOL_FP8
+
+
+def test_swiglu_epilogue_bit_exact_given_gate_up(dev):
+    """The SwiGLU -> NVFP4 epilogue reproduces the oracle's codes/scales from the kernel's own bf16 gate/up, and
+    gate/up themselves match the dequant matmul."""
+    M, K, F = 300, 256, 256
+    x = bf16_cpu((M, K), seed=11)
+    w = bf16_cpu((2 * F, K), seed=12, scale=0.05)
+    wc, ws, gw = quant_weight(w)
+    ga = onv.dynamic_act_global(float(x.float().abs().max()))
+    xc, xs = onv.quantize(x.float().numpy(), ga)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)   # noqa: E731
+    gu = torch.empty((M, 2 * F), dtype=torch.bfloat16, device=dev)
+    act_h = 0.002
+    hc, hs = _lib.gemm_nvfp4_swiglu(t(xc), t(onv.sf_tile(xs)), t(wc), t(onv.sf_tile(ws)), M, F, K, ga * gw, act_h,
+                                    gu_out=gu)
+    gu_ref = onv.bf16_round(onv.gemm(xc, xs, ga, wc, ws, gw))
+    assert rel_l2(f32(gu), gu_ref) <= TOL_NVFP4
+    h = ofu.swiglu(f32(gu))
+    rc, rs = onv.quantize(h, act_h)
+    np.testing.assert_array_equal(u8(hc), rc)
+    np.testing.assert_array_equal(u8(hs), onv.sf_tile(rs))
+
+
+def test_fused_mlp_config1(dev):
+    """X [4352, 3072] N(0,1); W_gu [16384, 3072], W_down [3072, 8192] N(0, 0.02); down.act from the
+    oracle's SwiGLU output with calibrate's 4x margin."""
+    M, K, F = 4352, 3072, 8192
+    x = bf16_cpu((M, K), seed=21)
+    wgu = bf16_cpu((2 * F, K), seed=22, scale=0.02)
+    wd = bf16_cpu((K, F), seed=23, scale=0.02)
+    guc, gus, ggu = quant_weight(wgu)
+    dc, ds, gd = quant_weight(wd)
+    ax = onv.dynamic_act_global(float(x.float().abs().max()))
+    gu_ref = onv.bf16_round(onv.gemm(*onv.quantize(x.float().numpy(), ax), ax, guc, gus, ggu))
+    h_ref = ofu.swiglu(gu_ref)
+    act_h = 4 * float(np.abs(h_ref).max()) / (6 * 448)
+    y_ref = onv.bf16_round(onv.gemm(*onv.quantize(h_ref, act_h), act_h, dc, ds, gd))
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)   # noqa: E731
+    y = _lib.mlp_nvfp4(x.to(dev), F, ax, t(guc), t(onv.sf_tile(gus)), ggu, t(dc), t(onv.sf_tile(ds)), gd, act_h)
+    assert rel_l2(f32(y), y_ref) <= TOL_NVFP4
+
+
+# ----------------------------------------------------------------------------------------- API-level (linear.py)
+def test_nvfp4_linear_dynamic_and_static(dev):
+    M, N, K = 333, 384, 512
+    w = bf16_cpu((N, K), seed=31, scale=0.02)
+    x = bf16_cpu((M, K), seed=32, outliers=4)
+    lin = L.Nvfp4Linear(w.to(dev))
+    wc, ws, gw = quant_weight(w)
+    np.testing.assert_array_equal(u8(lin.lin.codes), wc)          # nvfp4_weight through the GPU quantizer
+    np.testing.assert_array_equal(u8(lin.lin.scales()), ws)
+    assert lin.lin.scale == gw
+    y = lin(x.to(dev))
+    a = onv.dynamic_act_global(float(x.float().abs().max()))
+    assert lin.amax == a and lin.lin.act == a
+    assert rel_l2(f32(y), onv.linear(x.float().numpy(), wc, ws, gw, a)) <= TOL_NVFP4
+    lin.set_act(0.02)
+    y2 = lin(x.to(dev))
+    assert rel_l2(f32(y2), onv.linear(x.float().numpy(), wc, ws, gw, 0.02)) <= TOL_NVFP4
+
+
+def test_swiglu_mlp_api_and_fallback_contract(dev):
+    M, K, F = 256, 256, 384
+    gu = L.Nvfp4Linear(bf16_cpu((2 * F, K), seed=41, scale=0.05).to(dev))
+    down = L.Nvfp4Linear(bf16_cpu((K, F), seed=42, scale=0.05).to(dev))
+    x = bf16_cpu((M, K), seed=43).to(dev)
+    assert L.swiglu_mlp(gu, down, x) is None                         # dynamic layers: caller falls back
+    gu.set_act(0.004)
+    down.set_act(0.001)
+    y = L.swiglu_mlp(gu, down, x)
+    from tfimage import kernels as K
+    ref = down(K.swiglu(gu(x)))                                       # the unfused chain the model falls back to
+    assert rel_l2(f32(y), f32(ref)) <= TOL_NVFP4
+
+
+def test_fp8_linear_api(dev):
+    w = bf16_cpu((256, 384), seed=51, scale=0.02)
+    x = bf16_cpu((100, 384), seed=52)
+    for act, pc in ((None, False), (0.05, False), (None, True)):
+        lin = L.Fp8Linear(w.to(dev), act, per_channel=pc)
+        y = lin(x.to(dev))
+        w8, ws = ofp8.weight(w.float().numpy(), pc)
+        ref = ofp8.linear(x.float().numpy(), w8, ws, act)
+        assert rel_l2(f32(y), ref) <= TOL_FP8
