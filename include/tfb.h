@@ -88,12 +88,12 @@ tfb_status tfb_gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N
 
 /* Gate/up NVFP4 GEMM with a SwiGLU epilogue that writes NVFP4: W_gu = [gate; up] codes [2F, K].
  * h = bf16(bf16(silu(gate)) * up) with gate/up = bf16(alpha * acc), quantized under h_global into
- * h_codes [M, F/2] and h_sf (TFB_SF_TILED, rows = M, K = F). gu_out (nullable) receives the bf16 gate/up
- * [M, 2F] for testing. Replaces the first half of TensorFold checkpoint.mlp_prompt (tfimage/linear.py:150).
- * F % 128 == 0, K % 128 == 0. */
+ * h_codes [M, F/2] and h_sf (TFB_SF_TILED, rows = M, K = F). gu_out and h_out (both nullable) receive the
+ * bf16 gate/up [M, 2F] and the bf16 h [M, F] for testing. Replaces the first half of TensorFold
+ * checkpoint.mlp_prompt (tfimage/linear.py:150). F % 128 == 0, K % 128 == 0. */
 tfb_status tfb_gemm_nvfp4_swiglu(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* gu_codes,
                                  const uint8_t* gu_sf, int64_t M, int64_t F, int64_t K, float alpha, float h_global,
-                                 uint8_t* h_codes, uint8_t* h_sf, void* gu_out, void* stream);
+                                 uint8_t* h_codes, uint8_t* h_sf, void* gu_out, void* h_out, void* stream);
 
 /* Whole fused MLP pair (tfimage/linear.py:136-150, swiglu_mlp): quantize x [M, K] under act_x, gate/up GEMM with
  * the SwiGLU->NVFP4 epilogue under act_h, down GEMM -> y [M, K] bf16. The four ws_* buffers are caller-owned

@@ -1,13 +1,18 @@
 // tcgen05 GEMMs for sm_100a: NVFP4 W4A4 (kind::mxf4nvf4, E4M3 block scales per 16), FP8 W8A8 (kind::f8f6f4), and
 // the NVFP4 gate/up GEMM whose epilogue applies SwiGLU and writes NVFP4 rows + scales for the down projection.
 //
-// One persistent CTA per SM walks 128 x 256 output tiles. Warp roles (192 threads):
-//   warp 0 lane 0 : TMA producer -- A tile [128 rows x 128 B], B tile [256 rows x 128 B] (two 128-row boxes),
-//                   128-byte swizzle, plus the stage's scale chunks by 1-D bulk copies; STAGES-deep ring.
-//   warp 1        : allocates TMEM (512 columns); lane 0 issues tcgen05.cp (scales -> TMEM) and tcgen05.mma
-//                   (M=128, N=256, K=64 fp4 / 32 fp8 per instruction) into a 256-column fp32 accumulator.
-//   warps 2..5    : epilogue -- tcgen05.ld 32 columns at a time (warp w reads TMEM lanes 32*(w%4)..+31, one output
-//                   row per thread), scale, convert, store.
+// One persistent CTA per SM walks 128 x 256 output tiles (M fastest). Warp roles (448 threads, 14 warps):
+//   warp 0 lane 0 : TMA producer -- per stage an A tile [128 rows x 128 B] and a B tile [256 rows x 128 B] (two
+//                   128-row boxes), 128-byte swizzle, plus the stage's scale chunks by 1-D bulk copies.
+//   warp 1        : allocates TMEM (512 columns); lane 0 issues tcgen05.mma (M=128, N=256, K=64 fp4 / 32 fp8) into
+//                   a 256-column fp32 accumulator. Its waits poll with mbarrier.test_wait: a blocking try_wait on
+//                   the issue path costs ~128 cycles per stage, a quarter of the stage's MMA time.
+//   warps 2..5    : scale writers (NVFP4 modes) -- copy the stage's scales smem -> registers -> TMEM with
+//                   tcgen05.st (one warp per TMEM lane quadrant). tcgen05.cp of the same bytes serialises with the
+//                   MMAs and costs ~40% of the tensor time; tcgen05.st from four warps runs alongside them.
+//   warps 6..13   : epilogue, two warps per TMEM lane quadrant (warp w reads lanes 32*(w%4)..+31, one output row
+//                   per thread, each warp half of the columns). They drain the accumulator into registers, release
+//                   it to the MMA warp, then scale / convert / store while the next tile's MMAs run.
 // Every mbarrier wait is bounded (kWaitLimitNs); a wait that runs out records a code in the device error word,
 // the other roles see it and leave their loops, in-flight copies/MMAs are drained (bounded) and TMEM is freed.
 // No TMA multicast anywhere: each CTA loads its own operand tiles.
@@ -22,10 +27,12 @@ constexpr int A_BYTES = BM * BKB;             // 16 KB
 constexpr int B_BYTES = BN * BKB;             // 32 KB
 constexpr int SFA_BYTES = 4 * 512;            // 4 scale chunks (64 K-elements each) of 128 rows
 constexpr int SFB_BYTES = 2 * 4 * 512;        // two 128-row groups
-constexpr int THREADS = 192;
+constexpr int THREADS = 448;
+constexpr int EPI_WARP0 = 6, SF_WARP0 = 2;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t ACC_COL = 0;               // accumulator: columns [0, 256)
-constexpr uint32_t SF_COL = 256;              // scales: 2 buffers x 48 columns (SFA 4x4, SFB 4x8)
+constexpr uint32_t SF_COL = 256;              // scales: one 48-column buffer per stage (SFA 4 x 4, SFB 4 x 8)
+constexpr uint32_t SF_STAGE_COLS = 48;
 
 enum Mode { MODE_FP4 = 0, MODE_FP8 = 1, MODE_FP4_SWIGLU = 2 };
 
@@ -49,6 +56,7 @@ struct Params {
   uint8_t* h_codes;      // [M, F/2]
   uint8_t* h_sf;         // tiled, K = F
   __nv_bfloat16* gu_out; // optional [M, 2F]
+  __nv_bfloat16* h_out;  // optional [M, F]
   int* err;
 };
 
@@ -62,6 +70,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// Blocking probe (the thread may be suspended for a while inside it): for waits off the MMA issue path.
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -73,14 +82,27 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: false if the limit ran out (code recorded) or another role already aborted.
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  const uint32_t a = smem_u32(bar);
-  if (mbar_try(a, parity)) return true;
+// Non-blocking probe: returns at once (used where a wake-up delay would idle the tensor core).
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false if the limit ran out (code recorded) or another role already aborted. The first probe is
+// inlined; only a miss calls the out-of-line loop (a call on the MMA issue path costs ~270 cycles, and the
+// tensor core's instruction queue is only ~2 MMAs deep, so every stall of the issuing thread idles it).
+template <bool POLL>
+__device__ __noinline__ bool mbar_wait_slow(uint32_t a, uint32_t parity, int* err, int code) {
   const unsigned long long t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try(a, parity)) return true;
-    if ((it & 255) == 0) {
+    if (POLL ? mbar_test(a, parity) : mbar_try(a, parity)) return true;
+    if ((it & 1023) == 0) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
       if ((long long)(globaltimer() - t0) > kWaitLimitNs) {
         atomicCAS(err, 0, code);
@@ -88,6 +110,12 @@ __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
       }
     }
   }
+}
+template <bool POLL>
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  const uint32_t a = smem_u32(bar);
+  if (POLL ? mbar_test(a, parity) : mbar_try(a, parity)) return true;
+  return mbar_wait_slow<POLL>(a, parity, err, code);
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
@@ -114,11 +142,6 @@ __device__ __forceinline__ uint64_t desc_sw128(const void* p) {
   const uint64_t a = smem_u32(p);
   return ((a & 0x3FFFFull) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
-// Descriptor of a 32-row x 16-byte scale block (no swizzle, 8-row core matrices 128 B apart) for tcgen05.cp.
-__device__ __forceinline__ uint64_t desc_sf(const void* p) {
-  const uint64_t a = smem_u32(p);
-  return ((a & 0x3FFFFull) >> 4) | (1ull << 16) | (8ull << 32) | (1ull << 46);
-}
 
 // Instruction descriptors (M = 128, N = 256, both operands K-major, fp32 accumulate).
 //   block-scaled mxf4nvf4: A/B format E2M1 (1) at bits 7-9 / 10-12, scale format UE4M3 (0) at bit 23;
@@ -140,8 +163,52 @@ __device__ __forceinline__ void mma_fp8(uint32_t d, uint64_t a, uint64_t b, uint
       ::"r"(d), "l"(a), "l"(b), "r"(IDESC_FP8), "r"(acc)
       : "memory");
 }
-__device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t desc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
+
+// fence::after_thread_sync + 4 MMAs + the commit that frees the stage's smem slot, as one asm statement.
+__device__ __forceinline__ void stage4_fp4(uint32_t d, uint64_t da, uint64_t db, uint32_t sf, uint32_t acc0,
+                                           uint32_t empty_bar) {
+  asm volatile(
+      "{\n\t.reg .pred pa;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t.reg .b32 s1, s2, s3, t0, t1, t2, t3;\n\t"
+      "setp.ne.b32 pa, %5, 0;\n\t"
+      "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\t"
+      "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\t"
+      "add.u32 s1, %3, 4;\n\tadd.u32 s2, %3, 8;\n\tadd.u32 s3, %3, 12;\n\t"
+      "add.u32 t0, %3, 16;\n\tadd.u32 t1, %3, 24;\n\tadd.u32 t2, %3, 32;\n\tadd.u32 t3, %3, 40;\n\t"
+      "tcgen05.fence::after_thread_sync;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %6, [%3], [t0], pa;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], a1, b1, %6, [s1], [t1], 1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], a2, b2, %6, [s2], [t2], 1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], a3, b3, %6, [s3], [t3], 1;\n\t"
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%4];\n\t}"
+      ::"r"(d), "l"(da), "l"(db), "r"(sf), "r"(empty_bar), "r"(acc0), "r"(IDESC_FP4)
+      : "memory");
+}
+__device__ __forceinline__ void stage4_fp8(uint32_t d, uint64_t da, uint64_t db, uint32_t acc0, uint32_t empty_bar) {
+  asm volatile(
+      "{\n\t.reg .pred pa;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+      "setp.ne.b32 pa, %4, 0;\n\t"
+      "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\t"
+      "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\t"
+      "tcgen05.fence::after_thread_sync;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %5, pa;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], a1, b1, %5, 1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], a2, b2, %5, 1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], a3, b3, %5, 1;\n\t"
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%3];\n\t}"
+      ::"r"(d), "l"(da), "l"(db), "r"(empty_bar), "r"(acc0), "r"(IDESC_FP8)
+      : "memory");
+}
+
+// Warp-collective TMEM stores of this warp's 32 lanes: 4 and 8 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint4 v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, uint4 a, uint4 b) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(a.x),
+               "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+               : "memory");
 }
 
 // 32 consecutive fp32 columns of this thread's TMEM lane.
@@ -159,6 +226,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+
+// 16 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// silu(g) = g / (1 + e^-g) with the hardware exp2 and reciprocal approximations (the reference's Triton kernel
+// used approximate math too); the result is rounded to bf16 by the caller.
+__device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 __host__ __device__ constexpr int smem_bytes(int mode) {
   return 1024 /* alignment slack */ + STAGES * (A_BYTES + B_BYTES) +
@@ -178,7 +263,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* sSFB = sSFA + (FP4 ? STAGES * SFA_BYTES : 0);
   uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + (FP4 ? STAGES * SFB_BYTES : 0));
   uint64_t* empty = full + STAGES;
-  uint64_t* acc_full = empty + STAGES;
+  uint64_t* sf_full = empty + STAGES;
+  uint64_t* acc_full = sf_full + STAGES;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* drain = acc_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -188,9 +274,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
+      mbar_init(sf_full + s, 4);   // one arrival per scale warp
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 128);
+    mbar_init(acc_empty, 256);     // every epilogue thread
     mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -205,207 +292,322 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // ------------------------------------------------------------------------------------------- producer
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
-    int stage = 0;
-    uint32_t ph = 0;
-    uint32_t issued = 0;     // bit s: stage s was armed at least once
-    uint32_t last_ph = 0;    // bit s: parity of its last arming
-    bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-      const int mb = tile % p.num_m, nb = tile / p.num_m;
-      int rb0, rb1;
-      if (MODE == MODE_FP4_SWIGLU) {
-        rb0 = nb * 128;
-        rb1 = p.N + nb * 128;
-      } else {
-        rb0 = nb * BN;
-        rb1 = nb * BN + 128;
-      }
-      const int g0 = rb0 >> 7, g1 = rb1 >> 7;
-      for (int ks = 0; ks < p.num_ks; ++ks) {
-        if (!mbar_wait(empty + stage, ph ^ 1, p.err, 0x101)) {
-          ok = false;
-          break;
+  if (warp == 0) {
+    if (lane == 0) {
+      // ----------------------------------------------------------------------------------------- producer
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+      int stage = 0;
+      uint32_t ph = 0;
+      uint32_t issued = 0;     // bit s: stage s was armed at least once
+      uint32_t last_ph = 0;    // bit s: parity of its last arming
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const int mb = tile % p.num_m, nb = tile / p.num_m;
+        int rb0, rb1;
+        if (MODE == MODE_FP4_SWIGLU) {
+          rb0 = nb * 128;
+          rb1 = p.N + nb * 128;
+        } else {
+          rb0 = nb * BN;
+          rb1 = nb * BN + 128;
         }
-        uint32_t tx = A_BYTES + B_BYTES;
-        uint32_t sf_bytes = 0;
-        if (FP4) {
-          const int kb_here = min(4, p.kb_total - ks * 4);
-          sf_bytes = kb_here * 512;
-          tx += sf_bytes * (1 + (g0 < p.sfb_groups) + (g1 < p.sfb_groups));
-        }
-        mbar_expect_tx(full + stage, tx);
-        tma_load_2d(sA + stage * A_BYTES, &tmA, full + stage, ks * BKB, mb * BM);
-        tma_load_2d(sB + stage * B_BYTES, &tmB, full + stage, ks * BKB, rb0);
-        tma_load_2d(sB + stage * B_BYTES + 128 * BKB, &tmB, full + stage, ks * BKB, rb1);
-        if (FP4) {
-          const size_t chunk = (size_t)ks * 4;
-          bulk_load(sSFA + stage * SFA_BYTES, p.sfa + ((size_t)mb * p.sf_chunks + chunk) * 512, sf_bytes,
-                    full + stage);
-          if (g0 < p.sfb_groups)
-            bulk_load(sSFB + stage * SFB_BYTES, p.sfb + ((size_t)g0 * p.sf_chunks + chunk) * 512, sf_bytes,
+        const int g0 = rb0 >> 7, g1 = rb1 >> 7;
+        for (int ks = 0; ks < p.num_ks; ++ks) {
+          if (!mbar_wait<false>(empty + stage, ph ^ 1, p.err, 0x101)) {
+            ok = false;
+            break;
+          }
+          uint32_t tx = A_BYTES + B_BYTES;
+          uint32_t sf_bytes = 0;
+          if (FP4) {
+            const int kb_here = min(4, p.kb_total - ks * 4);
+            sf_bytes = kb_here * 512;
+            tx += sf_bytes * (1 + (g0 < p.sfb_groups) + (g1 < p.sfb_groups));
+          }
+          mbar_expect_tx(full + stage, tx);
+          tma_load_2d(sA + stage * A_BYTES, &tmA, full + stage, ks * BKB, mb * BM);
+          tma_load_2d(sB + stage * B_BYTES, &tmB, full + stage, ks * BKB, rb0);
+          tma_load_2d(sB + stage * B_BYTES + 128 * BKB, &tmB, full + stage, ks * BKB, rb1);
+          if (FP4) {
+            const size_t chunk = (size_t)ks * 4;
+            bulk_load(sSFA + stage * SFA_BYTES, p.sfa + ((size_t)mb * p.sf_chunks + chunk) * 512, sf_bytes,
                       full + stage);
-          if (g1 < p.sfb_groups)
-            bulk_load(sSFB + stage * SFB_BYTES + 2048, p.sfb + ((size_t)g1 * p.sf_chunks + chunk) * 512, sf_bytes,
-                      full + stage);
-        }
-        issued |= 1u << stage;
-        last_ph = (last_ph & ~(1u << stage)) | (ph << stage);
-        if (++stage == STAGES) {
-          stage = 0;
-          ph ^= 1;
-        }
-      }
-    }
-    if (!ok) {  // let every copy already in flight land before the CTA exits
-      for (int s = 0; s < STAGES; ++s)
-        if (issued & (1u << s)) {
-          const uint32_t a = smem_u32(full + s);
-          const unsigned long long t0 = globaltimer();
-          while (!mbar_try(a, (last_ph >> s) & 1) && (long long)(globaltimer() - t0) < kWaitLimitNs) {
+            if (g0 < p.sfb_groups)
+              bulk_load(sSFB + stage * SFB_BYTES, p.sfb + ((size_t)g0 * p.sf_chunks + chunk) * 512, sf_bytes,
+                        full + stage);
+            if (g1 < p.sfb_groups)
+              bulk_load(sSFB + stage * SFB_BYTES + 2048, p.sfb + ((size_t)g1 * p.sf_chunks + chunk) * 512, sf_bytes,
+                        full + stage);
+          }
+          issued |= 1u << stage;
+          last_ph = (last_ph & ~(1u << stage)) | (ph << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            ph ^= 1;
           }
         }
-    }
-  } else if (warp == 1 && lane == 0) {
-    // ----------------------------------------------------------------------------------------------- MMA
-    int stage = 0;
-    uint32_t ph = 0, acc_ph = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-      if (!mbar_wait(acc_empty, acc_ph ^ 1, p.err, 0x201)) {
-        ok = false;
-        break;
       }
-      tc_fence_after();
-      for (int ks = 0; ks < p.num_ks; ++ks) {
-        if (!mbar_wait(full + stage, ph, p.err, 0x202)) {
+      if (!ok) {  // let every copy already in flight land before the CTA exits
+        for (int s = 0; s < STAGES; ++s)
+          if (issued & (1u << s)) {
+            const uint32_t a = smem_u32(full + s);
+            const unsigned long long t0 = globaltimer();
+            while (!mbar_try(a, (last_ph >> s) & 1) && (long long)(globaltimer() - t0) < kWaitLimitNs) {
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // --------------------------------------------------------------------------------------------- MMA
+      // Kept lean: between the last MMA of a stage and the first of the next the thread has about one MMA's
+      // execution time (~128 cycles) before the tensor core idles, so descriptors and TMEM addresses are
+      // precomputed and both barrier probes of a stage go out in one asm statement.
+      // Everything per stage slot is precomputed; the K loop runs in whole turns of the STAGES-slot ring with the
+      // slot index a compile-time constant, so a stage costs two barrier probes and one asm statement.
+      uint64_t dA[STAGES], dB[STAGES];
+      uint32_t fb[STAGES], sb[STAGES], eb[STAGES], sft[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) {
+        dA[s] = desc_sw128(sA + s * A_BYTES);
+        dB[s] = desc_sw128(sB + s * B_BYTES);
+        fb[s] = smem_u32(full + s);
+        sb[s] = smem_u32(sf_full + s);
+        eb[s] = smem_u32(empty + s);
+        sft[s] = tmem + SF_COL + s * SF_STAGE_COLS;
+      }
+      const uint32_t dacc = tmem + ACC_COL;
+      int stage = 0;                           // ring slot of the next stage (tiles need not start at slot 0)
+      uint32_t ph = 0, acc_ph = 0;
+      bool ok = true;
+      auto stage_ready = [&](int s, uint32_t par) -> bool {
+        uint32_t r;
+        if (FP4) {
+          asm volatile(
+              "{\n\t.reg .pred p, q;\n\t"
+              "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %3;\n\t"
+              "mbarrier.test_wait.parity.shared::cta.b64 q, [%2], %3;\n\t"
+              "and.pred p, p, q;\n\t"
+              "selp.u32 %0, 1, 0, p;\n\t}"
+              : "=r"(r)
+              : "r"(fb[s]), "r"(sb[s]), "r"(par)
+              : "memory");
+        } else {
+          r = mbar_test(fb[s], par);
+        }
+        if (r) return true;
+        return mbar_wait_slow<true>(fb[s], par, p.err, 0x202) &&
+               (!FP4 || mbar_wait_slow<true>(sb[s], par, p.err, 0x203));
+      };
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        if (!mbar_wait<true>(acc_empty, acc_ph ^ 1, p.err, 0x201)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int kb_here = min(4, p.kb_total - ks * 4);
-        const uint32_t sfa_t = tmem + SF_COL + (stage & 1) * 48;
-        const uint32_t sfb_t = sfa_t + 16;
-        if (FP4) {
-          for (int kb = 0; kb < kb_here; ++kb) {
-            tc_cp_sf(sfa_t + kb * 4, desc_sf(sSFA + stage * SFA_BYTES + kb * 512));
-            tc_cp_sf(sfb_t + kb * 8, desc_sf(sSFB + stage * SFB_BYTES + kb * 512));
-            tc_cp_sf(sfb_t + kb * 8 + 4, desc_sf(sSFB + stage * SFB_BYTES + 2048 + kb * 512));
+        int ks = 0;
+        const int full_stages = p.kb_total >> 2;           // stages with all 4 MMA k-blocks
+        // align to the ring so that the unrolled turns below start at slot 0
+        while (ok && stage != 0 && ks < full_stages) {
+          if (!stage_ready(stage, ph)) { ok = false; break; }
+          if (FP4) stage4_fp4(dacc, dA[stage], dB[stage], sft[stage], ks != 0, eb[stage]);
+          else stage4_fp8(dacc, dA[stage], dB[stage], ks != 0, eb[stage]);
+          ++ks;
+          if (++stage == STAGES) { stage = 0; ph ^= 1; }
+        }
+        while (ok && ks + STAGES <= full_stages) {
+#pragma unroll
+          for (int s = 0; s < STAGES; ++s) {
+            if (!stage_ready(s, ph)) { ok = false; break; }
+            if (FP4) stage4_fp4(dacc, dA[s], dB[s], sft[s], (ks + s) != 0, eb[s]);
+            else stage4_fp8(dacc, dA[s], dB[s], (ks + s) != 0, eb[s]);
           }
-        }
-        for (int kb = 0; kb < kb_here; ++kb) {
-          const uint64_t da = desc_sw128(sA + stage * A_BYTES + kb * 32);
-          const uint64_t db = desc_sw128(sB + stage * B_BYTES + kb * 32);
-          const uint32_t acc = (ks | kb) != 0;
-          if (FP4)
-            mma_fp4(tmem + ACC_COL, da, db, sfa_t + kb * 4, sfb_t + kb * 8, acc);
-          else
-            mma_fp8(tmem + ACC_COL, da, db, acc);
-        }
-        tc_commit(empty + stage);
-        if (++stage == STAGES) {
-          stage = 0;
+          ks += STAGES;
           ph ^= 1;
         }
+        while (ok && ks < p.num_ks) {                     // the remaining stages (and a partial last one)
+          if (!stage_ready(stage, ph)) { ok = false; break; }
+          const int kb_here = min(4, p.kb_total - ks * 4);
+          if (kb_here == 4) {
+            if (FP4) stage4_fp4(dacc, dA[stage], dB[stage], sft[stage], ks != 0, eb[stage]);
+            else stage4_fp8(dacc, dA[stage], dB[stage], ks != 0, eb[stage]);
+          } else {
+            tc_fence_after();
+            for (int kb = 0; kb < kb_here; ++kb) {
+              const uint32_t acc = (ks | kb) != 0;
+              if (FP4)
+                mma_fp4(dacc, dA[stage] + 2 * kb, dB[stage] + 2 * kb, sft[stage] + kb * 4, sft[stage] + 16 + kb * 8,
+                        acc);
+              else
+                mma_fp8(dacc, dA[stage] + 2 * kb, dB[stage] + 2 * kb, acc);
+            }
+            tc_commit(empty + stage);
+          }
+          ++ks;
+          if (++stage == STAGES) { stage = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(acc_full);
+        acc_ph ^= 1;
       }
-      if (!ok) break;
-      tc_commit(acc_full);
-      acc_ph ^= 1;
+      // drain: the commit arrives once every tcgen05 op this thread issued has completed
+      tc_commit(drain);
+      const uint32_t a = smem_u32(drain);
+      const unsigned long long t0 = globaltimer();
+      while (!mbar_try(a, 0) && (long long)(globaltimer() - t0) < kWaitLimitNs) {
+      }
     }
-    // drain: the commit arrives once every tcgen05 op this thread issued has completed
-    tc_commit(drain);
-    const uint32_t a = smem_u32(drain);
-    const unsigned long long t0 = globaltimer();
-    while (!mbar_try(a, 0) && (long long)(globaltimer() - t0) < kWaitLimitNs) {
+  } else if (warp < EPI_WARP0) {
+    // ------------------------------------------------------------------------------------------ scale writers
+    // Lane r of quadrant q writes TMEM lane 32q + r: for SFA the 16 bytes at r * 16 of each 512-byte chunk (rows
+    // r, r+32, r+64, r+96 x 4 scales), for SFB the same from the two 128-row groups (8 columns). Every quadrant
+    // holds the same values: the block-scaled MMA reads the copy of its own lane quadrant.
+    if (FP4) {
+      const uint32_t q = warp & 3;
+      const uint32_t tq = tmem + ((q * 32) << 16);
+      int stage = 0;
+      uint32_t ph = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+        bool ok = true;
+        for (int ks = 0; ks < p.num_ks; ++ks) {
+          if (!mbar_wait<false>(full + stage, ph, p.err, 0x401)) {
+            ok = false;
+            break;
+          }
+          const int kb_here = min(4, p.kb_total - ks * 4);
+          const uint4* a4 = reinterpret_cast<const uint4*>(sSFA + stage * SFA_BYTES) + lane;
+          const uint4* b4 = reinterpret_cast<const uint4*>(sSFB + stage * SFB_BYTES) + lane;
+          const uint32_t col = SF_COL + stage * SF_STAGE_COLS;
+          for (int kb = 0; kb < kb_here; ++kb) {
+            tmem_st4(tq + col + kb * 4, a4[kb * 32]);
+            tmem_st8(tq + col + 16 + kb * 8, b4[kb * 32], b4[128 + kb * 32]);
+          }
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(sf_full + stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
     }
-  } else if (warp >= 2) {
+  } else {
     // ------------------------------------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const int r = q * 32 + lane;               // row inside the tile == TMEM lane
+    const int half = (warp - EPI_WARP0) >> 2;      // which half of the tile's columns this warp drains
+    const int r = q * 32 + lane;                   // row inside the tile == TMEM lane
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
     uint32_t acc_ph = 0;
-    const Nvfp4Enc enc = nvfp4_enc(MODE == MODE_FP4_SWIGLU ? p.h_g : 1.0f);
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-      if (!mbar_wait(acc_full, acc_ph, p.err, 0x301)) break;
+      if (!mbar_wait<false>(acc_full, acc_ph, p.err, 0x301)) break;
       tc_fence_after();
       const int mb = tile % p.num_m, nb = tile / p.num_m;
       const int64_t m = (int64_t)mb * BM + r;
       if (MODE == MODE_FP4_SWIGLU) {
+        // this warp: hidden columns [half*64, half*64 + 64) of the tile = gate and up accumulator columns
         const int F = p.N;
+        const int64_t col0 = (int64_t)nb * 128 + half * 64;
+        uint32_t hp[32];                           // 64 bf16 h values, packed in pairs
+#pragma unroll
         for (int c = 0; c < 4; ++c) {
-          float g[32], u[32];
-          tmem_ld32(trow + ACC_COL + c * 32, g);
-          tmem_ld32(trow + ACC_COL + 128 + c * 32, u);
-          if (c == 3) {
-            tc_fence_before();
-            mbar_arrive(acc_empty);
+          float g[16], u[16];
+          tmem_ld16(trow + ACC_COL + half * 64 + c * 16, g);
+          tmem_ld16(trow + ACC_COL + 128 + half * 64 + c * 16, u);
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            const float g0 = bf16_round(g[j] * p.alpha), g1 = bf16_round(g[j + 1] * p.alpha);
+            const float u0 = bf16_round(u[j] * p.alpha), u1 = bf16_round(u[j + 1] * p.alpha);
+            g[j] = g0;
+            g[j + 1] = g1;
+            u[j] = u0;
+            u[j + 1] = u1;
+            hp[c * 8 + j / 2] = pack_bf16x2(bf16_round(silu_fast(g0)) * u0, bf16_round(silu_fast(g1)) * u1);
           }
-          const int64_t col = (int64_t)nb * 128 + c * 32;  // hidden column of g[0]
-          if (m < p.M) {
-            float h[32];
+          if (p.gu_out && m < p.M) {
+            uint4* dg = reinterpret_cast<uint4*>(p.gu_out + m * 2 * F + col0 + c * 16);
+            uint4* du = reinterpret_cast<uint4*>(p.gu_out + m * 2 * F + F + col0 + c * 16);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float gv = bf16_round(g[j] * p.alpha), uv = bf16_round(u[j] * p.alpha);
-              g[j] = gv;
-              u[j] = uv;
-              h[j] = bf16_round(bf16_round(__fdiv_rn(gv, 1.0f + expf(-gv))) * uv);
+            for (int v = 0; v < 2; ++v) {
+              dg[v] = make_uint4(pack_bf16x2(g[8 * v], g[8 * v + 1]), pack_bf16x2(g[8 * v + 2], g[8 * v + 3]),
+                                 pack_bf16x2(g[8 * v + 4], g[8 * v + 5]), pack_bf16x2(g[8 * v + 6], g[8 * v + 7]));
+              du[v] = make_uint4(pack_bf16x2(u[8 * v], u[8 * v + 1]), pack_bf16x2(u[8 * v + 2], u[8 * v + 3]),
+                                 pack_bf16x2(u[8 * v + 4], u[8 * v + 5]), pack_bf16x2(u[8 * v + 6], u[8 * v + 7]));
             }
-            if (p.gu_out) {
-              uint4* dg = reinterpret_cast<uint4*>(p.gu_out + m * 2 * F + col);
-              uint4* du = reinterpret_cast<uint4*>(p.gu_out + m * 2 * F + F + col);
-#pragma unroll
-              for (int v = 0; v < 4; ++v) {
-                dg[v] = make_uint4(pack_bf16x2(g[8 * v], g[8 * v + 1]), pack_bf16x2(g[8 * v + 2], g[8 * v + 3]),
-                                   pack_bf16x2(g[8 * v + 4], g[8 * v + 5]), pack_bf16x2(g[8 * v + 6], g[8 * v + 7]));
-                du[v] = make_uint4(pack_bf16x2(u[8 * v], u[8 * v + 1]), pack_bf16x2(u[8 * v + 2], u[8 * v + 3]),
-                                   pack_bf16x2(u[8 * v + 4], u[8 * v + 5]), pack_bf16x2(u[8 * v + 6], u[8 * v + 7]));
-              }
-            }
-            uint32_t sfv[2], cw[4];
-#pragma unroll
-            for (int blk = 0; blk < 2; ++blk) {
-              float amax = 0.0f;
-#pragma unroll
-              for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(h[16 * blk + j]));
-              sfv[blk] = nvfp4_scale(amax, enc);
-              const float inv = nvfp4_inv(sfv[blk], enc);
-              cw[2 * blk] = nvfp4_codes8(h + 16 * blk, inv);
-              cw[2 * blk + 1] = nvfp4_codes8(h + 16 * blk + 8, inv);
-            }
-            *reinterpret_cast<uint4*>(p.h_codes + m * (F / 2) + col / 2) = make_uint4(cw[0], cw[1], cw[2], cw[3]);
-            *reinterpret_cast<uint16_t*>(p.h_sf + sf_tiled_offset(m, col / 16, F / 64)) =
-                (uint16_t)(sfv[0] | (sfv[1] << 8));
-          } else {
-            *reinterpret_cast<uint16_t*>(p.h_sf + sf_tiled_offset(m, col / 16, F / 64)) = 0;
           }
         }
+        tc_fence_before();
+        mbar_arrive(acc_empty);                    // accumulator drained: the next tile's MMAs may start
+        if (m < p.M) {
+          if (p.h_out) {
+            uint4* dh = reinterpret_cast<uint4*>(p.h_out + m * F + col0);
+#pragma unroll
+            for (int v = 0; v < 8; ++v) dh[v] = make_uint4(hp[4 * v], hp[4 * v + 1], hp[4 * v + 2], hp[4 * v + 3]);
+          }
+          const Nvfp4Enc enc = nvfp4_enc(p.h_g);
+          uint32_t cw[8], sfw = 0;
+#pragma unroll
+          for (int blk = 0; blk < 4; ++blk) {
+            float h[16];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              h[2 * j] = __uint_as_float(hp[blk * 8 + j] << 16);
+              h[2 * j + 1] = __uint_as_float(hp[blk * 8 + j] & 0xFFFF0000u);
+            }
+            float amax = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(h[j]));
+            const uint32_t sf = nvfp4_scale(amax, enc);
+            const float inv = nvfp4_inv(sf, enc);
+            cw[2 * blk] = nvfp4_codes8(h, inv);
+            cw[2 * blk + 1] = nvfp4_codes8(h + 8, inv);
+            sfw |= sf << (8 * blk);
+          }
+          uint4* dc = reinterpret_cast<uint4*>(p.h_codes + m * (F / 2) + col0 / 2);
+          dc[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+          dc[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
+          *reinterpret_cast<uint32_t*>(p.h_sf + sf_tiled_offset(m, col0 / 16, F / 64)) = sfw;
+        } else {
+          *reinterpret_cast<uint32_t*>(p.h_sf + sf_tiled_offset(m, col0 / 16, F / 64)) = 0u;
+        }
       } else {
+        // this warp: output columns [half*128, half*128 + 128) of the tile
         float scale = p.alpha;
         if (MODE == MODE_FP8) scale = __ldg(p.a_scale) * (p.b_per_channel ? 1.0f : __ldg(p.b_scale));
+        const int64_t n_base = (int64_t)nb * BN + half * 128;
+        uint32_t pk[64];
+#pragma unroll
         for (int c = 0; c < 8; ++c) {
-          float v[32];
-          tmem_ld32(trow + ACC_COL + c * 32, v);
-          if (c == 7) {
-            tc_fence_before();
-            mbar_arrive(acc_empty);
+          float v[16];
+          tmem_ld16(trow + ACC_COL + half * 128 + c * 16, v);
+          const int64_t n0 = n_base + c * 16;
+          if (MODE == MODE_FP8 && p.b_per_channel) {
+            const bool inb = n0 < p.N;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] *= scale * (inb ? __ldg(p.b_scale + n0 + j) : 0.0f);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] *= scale;
           }
-          const int64_t n0 = (int64_t)nb * BN + c * 32;
-          if (m < p.M && n0 < p.N) {
-            if (MODE == MODE_FP8 && p.b_per_channel) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] *= scale * __ldg(p.b_scale + n0 + j);
-            } else {
+          for (int j = 0; j < 8; ++j) pk[c * 8 + j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+        }
+        tc_fence_before();
+        mbar_arrive(acc_empty);                    // accumulator drained: the next tile's MMAs may start
+        if (m < p.M) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] *= scale;
+          for (int c = 0; c < 4; ++c) {
+            const int64_t n0 = n_base + c * 32;
+            if (n0 < p.N) {
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.y) + m * p.ldy + n0);
+#pragma unroll
+              for (int t = 0; t < 4; ++t)
+                dst[t] = make_uint4(pk[c * 16 + 4 * t], pk[c * 16 + 4 * t + 1], pk[c * 16 + 4 * t + 2],
+                                    pk[c * 16 + 4 * t + 3]);
             }
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.y) + m * p.ldy + n0);
-#pragma unroll
-            for (int t = 0; t < 4; ++t)
-              dst[t] = make_uint4(pack_bf16x2(v[8 * t], v[8 * t + 1]), pack_bf16x2(v[8 * t + 2], v[8 * t + 3]),
-                                  pack_bf16x2(v[8 * t + 4], v[8 * t + 5]), pack_bf16x2(v[8 * t + 6], v[8 * t + 7]));
           }
         }
       }
@@ -488,13 +690,13 @@ tfb_status gemm_nvfp4(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, c
 
 tfb_status gemm_nvfp4_swiglu(const uint8_t* a, const uint8_t* a_sf, const uint8_t* gu, const uint8_t* gu_sf, int64_t M,
                              int64_t F, int64_t K, float alpha, float h_g, uint8_t* h_codes, uint8_t* h_sf,
-                             void* gu_out, cudaStream_t s) {
+                             void* gu_out, void* h_out, cudaStream_t s) {
   tfb_status st = check_common(M, F, K, "gemm_nvfp4_swiglu");
   if (st != TFB_OK) return st;
   if (F % 128) return fail(TFB_BAD_SHAPE, "gemm_nvfp4_swiglu: F=%lld must be a multiple of 128", (long long)F);
   if (!(h_g > 0.0f) || !isfinite(h_g)) return fail(TFB_BAD_ARG, "gemm_nvfp4_swiglu: h_global must be positive");
   if (!aligned(h_codes, 16) || !aligned(h_sf, 16) || !aligned(a_sf, 16) || !aligned(gu_sf, 16) ||
-      (gu_out && !aligned(gu_out, 16)))
+      (gu_out && !aligned(gu_out, 16)) || (h_out && !aligned(h_out, 16)))
     return fail(TFB_BAD_ALIGN, "gemm_nvfp4_swiglu: outputs and scales must be 16-byte aligned");
   const DeviceInfo* di;
   if ((st = device_info(&di)) != TFB_OK) return st;
@@ -518,6 +720,7 @@ tfb_status gemm_nvfp4_swiglu(const uint8_t* a, const uint8_t* a_sf, const uint8_
   p.h_codes = h_codes;
   p.h_sf = h_sf;
   p.gu_out = static_cast<__nv_bfloat16*>(gu_out);
+  p.h_out = static_cast<__nv_bfloat16*>(h_out);
   p.err = di->err_word;
   return launch<MODE_FP4_SWIGLU>(ta, tb, p, s);
 }
@@ -566,8 +769,8 @@ tfb_status tfb_gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N
 
 tfb_status tfb_gemm_nvfp4_swiglu(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* gu_codes,
                                  const uint8_t* gu_sf, int64_t M, int64_t F, int64_t K, float alpha, float h_global,
-                                 uint8_t* h_codes, uint8_t* h_sf, void* gu_out, void* stream) {
-  return tfb::gemm_nvfp4_swiglu(a_codes, a_sf, gu_codes, gu_sf, M, F, K, alpha, h_global, h_codes, h_sf, gu_out,
+                                 uint8_t* h_codes, uint8_t* h_sf, void* gu_out, void* h_out, void* stream) {
+  return tfb::gemm_nvfp4_swiglu(a_codes, a_sf, gu_codes, gu_sf, M, F, K, alpha, h_global, h_codes, h_sf, gu_out, h_out,
                                 static_cast<cudaStream_t>(stream));
 }
 
@@ -579,7 +782,7 @@ tfb_status tfb_mlp_nvfp4(const void* x, int64_t M, int64_t K, int64_t F, float a
   tfb_status st = tfb::quant_nvfp4(x, M, K, K, act_x, ws_xc, ws_xsf, TFB_SF_TILED, s);
   if (st != TFB_OK) return st;
   st = tfb::gemm_nvfp4_swiglu(ws_xc, ws_xsf, gu_codes, gu_sf, M, F, K, (float)((double)act_x * g_gu), act_h, ws_hc,
-                              ws_hsf, nullptr, s);
+                              ws_hsf, nullptr, nullptr, s);
   if (st != TFB_OK) return st;
   return tfb::gemm_nvfp4(ws_hc, ws_hsf, down_codes, down_sf, M, K, F, (float)((double)act_h * g_down), y, K, s);
 }

@@ -31,7 +31,8 @@ SIGNATURES = {
     "tfb_quant_fp8": [c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp],
     "tfb_gemm_nvfp4": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_vp, c_i64, c_vp],
     "tfb_gemm_fp8": [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_int, c_vp, c_i64, c_vp],
-    "tfb_gemm_nvfp4_swiglu": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_float, c_vp, c_vp, c_vp, c_vp],
+    "tfb_gemm_nvfp4_swiglu": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_float, c_vp, c_vp, c_vp, c_vp,
+                              c_vp],
     "tfb_mlp_nvfp4": [c_vp, c_i64, c_i64, c_i64, c_float, c_vp, c_vp, c_float, c_vp, c_vp, c_float, c_float, c_vp,
                       c_vp, c_vp, c_vp, c_vp, c_vp],
     "tfb_adaln": [c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_float, c_vp, c_float, c_vp, c_vp, c_vp],
@@ -169,7 +170,7 @@ def gemm_fp8(a8, b8, M: int, N: int, K: int, a_scale, b_scale, out=None) -> torc
 
 
 def gemm_nvfp4_swiglu(a_codes, a_sf, gu_codes, gu_sf, M: int, F: int, K: int, alpha: float, h_global: float,
-                      h_codes=None, h_sf=None, gu_out=None):
+                      h_codes=None, h_sf=None, gu_out=None, h_out=None):
     _cuda(a_codes, a_sf, gu_codes, gu_sf)
     dev = a_codes.device
     if h_codes is None:
@@ -178,7 +179,7 @@ def gemm_nvfp4_swiglu(a_codes, a_sf, gu_codes, gu_sf, M: int, F: int, K: int, al
         h_sf = torch.empty((sf_tiled_bytes(M, F),), dtype=torch.uint8, device=dev)
     check(load().tfb_gemm_nvfp4_swiglu(a_codes.data_ptr(), a_sf.data_ptr(), gu_codes.data_ptr(), gu_sf.data_ptr(), M, F,
                                        K, float(alpha), float(h_global), h_codes.data_ptr(), h_sf.data_ptr(),
-                                       _ptr(gu_out), _stream(a_codes)))
+                                       _ptr(gu_out), _ptr(h_out), _stream(a_codes)))
     return h_codes, h_sf
 
 
