@@ -36,10 +36,25 @@ FLOP_DOWN = 2 * M_ROWS * F_DIM * K_DIM            # 219.04 GFLOP
 FLOP_STEP = FLOP_GU + FLOP_DOWN
 FP4_TO_BF16 = 4.0                                  # B200 dense FP4 : BF16 tensor rate (9 : 2.25 PFLOP/s)
 # DRAM bytes per gate/up launch (dram__bytes_read.sum + dram__bytes_write.sum) from the ncu capture summarised in
-# profiles/gemm_nvfp4_swiglu_config1.md; None until measured.
-TRAFFIC_GU = None
+# profiles/gemm_nvfp4_config1.md.
+TRAFFIC_GU = 36.18e6
 WORKLOAD = ("configs[1] fused NVFP4 MLP pair: X bf16 [4352,3072] N(0,1) -> gate/up W [16384,3072] N(0,0.02) with "
             "SwiGLU->NVFP4 epilogue -> down W [3072,8192] N(0,0.02) -> bf16 [4352,3072]")
+
+
+def fp4_issue_peak():
+    """Dense FP4 MMA ceiling measured live by csrc/mma_peak_probe.cu (built by build.py --probe), or None."""
+    import re
+    import subprocess
+    exe = ROOT / "qwen-image21-tensorfold-rtx_b200" / "_build" / "mma_peak_probe"
+    if not exe.exists():
+        return None
+    try:
+        out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60).stdout
+        m = re.search(r"mxf4nvf4.*?([0-9.]+) cycles/MMA\s+([0-9.]+) TFLOP/s", out)
+        return (float(m.group(2)), float(m.group(1))) if m else None
+    except (OSError, subprocess.SubprocessError):
+        return None
 
 
 def peaks():
@@ -286,7 +301,16 @@ def run_ours(args):
 
     if rank == 0:
         pk, src = peaks()
-        fp4_peak = FP4_TO_BF16 * pk["bf16_tflops"]
+        derived = FP4_TO_BF16 * pk["bf16_tflops"]
+        probe = fp4_issue_peak()
+        if probe:
+            fp4_peak = probe[0]
+            peak_note = (f"measured: tcgen05 mxf4nvf4 M128xN256xK64 issue-rate probe, {probe[1]:.1f} cycles/MMA, "
+                         f"{probe[0]:.0f} TFLOP/s (csrc/mma_peak_probe.cu); 4 x measured bf16 burst = {derived:.0f}; "
+                         f"nominal 9000")
+        else:
+            fp4_peak = derived
+            peak_note = f"4 x bf16 burst {pk['bf16_tflops']} TFLOP/s ({src}); nominal 9000"
         gu_ms = statistics.median(p[1] for p in per)
         down_ms = statistics.median(p[2] for p in per)
         q_ms = statistics.median(p[0] for p in per)
@@ -298,13 +322,12 @@ def run_ours(args):
             "config": {"workload": WORKLOAD, "M": M_ROWS, "K": K_DIM, "F": F_DIM, "global_batch": world,
                        "rows_per_gpu": M_ROWS, "parallelism": f"dp{world} (independent images, no collective)",
                        "l2": "flushed between steps: 256 MiB write outside the per-step events"},
-            "pct_fp4_peak": value / world / fp4_peak,
+            "pct_fp4_peak": value / world / fp4_peak, "pct_fp4_nominal": value / world / 9000.0,
             "kernels_ms": {"quant_x": q_ms, "gate_up_swiglu_nvfp4": gu_ms, "down": down_ms},
             "roofline": {"bound": "tensor", "kernel": "gemm_kernel<MODE_FP4_SWIGLU> (gate/up + SwiGLU->NVFP4)",
                          "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s", "frac": achieved / fp4_peak,
-                         "traffic": TRAFFIC_GU,
-                         "peak_note": f"dense FP4 = {FP4_TO_BF16:g} x bf16 burst {pk['bf16_tflops']} TFLOP/s "
-                                      f"({src}); nominal 9000"},
+                         "traffic": TRAFFIC_GU, "traffic_unit": "bytes per launch",
+                         "frac_of_nominal_9000": achieved / 9000.0, "peak_note": peak_note},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": x_host.numel() * 2,
                     "d2h_bytes_per_step": y_host.numel() * 2},
             "gpu_launches": 3 * args.steps,
