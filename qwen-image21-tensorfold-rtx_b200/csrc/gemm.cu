@@ -3,16 +3,19 @@
 //
 // One persistent CTA per SM walks 128 x 256 output tiles (M fastest). Warp roles (448 threads, 14 warps):
 //   warp 0 lane 0 : TMA producer -- per stage an A tile [128 rows x 128 B] and a B tile [256 rows x 128 B] (two
-//                   128-row boxes), 128-byte swizzle, plus the stage's scale chunks by 1-D bulk copies.
+//                   128-row boxes), 128-byte swizzle.
 //   warp 1        : allocates TMEM (512 columns); lane 0 issues tcgen05.mma (M=128, N=256, K=64 fp4 / 32 fp8) into
 //                   a 256-column fp32 accumulator. Its waits poll with mbarrier.test_wait: a blocking try_wait on
 //                   the issue path costs ~128 cycles per stage, a quarter of the stage's MMA time.
-//   warps 2..5    : scale writers (NVFP4 modes) -- copy the stage's scales smem -> registers -> TMEM with
-//                   tcgen05.st (one warp per TMEM lane quadrant). tcgen05.cp of the same bytes serialises with the
-//                   MMAs and costs ~40% of the tensor time; tcgen05.st from four warps runs alongside them.
+//   warps 2..5    : scale writers (NVFP4 modes) -- load the stage's scales from global memory into registers and
+//                   write them to TMEM with tcgen05.st (one warp per TMEM lane quadrant). tcgen05.cp of the same
+//                   bytes serialises with the MMAs and costs ~40% of the tensor time; tcgen05.st from four warps
+//                   runs alongside them.
 //   warps 6..13   : epilogue, two warps per TMEM lane quadrant (warp w reads lanes 32*(w%4)..+31, one output row
 //                   per thread, each warp half of the columns). They drain the accumulator into registers, release
-//                   it to the MMA warp, then scale / convert / store while the next tile's MMAs run.
+//                   it to the MMA warp, then scale / convert / store while the next tile's MMAs run. bf16 outputs
+//                   go through a 128-byte-swizzled smem box per warp and TMA tensor stores: per-row 16-byte global
+//                   stores crowd the memory-instruction path the MMA issue shares and stalled it ~4500 cycles/tile.
 // Every mbarrier wait is bounded (kWaitLimitNs); a wait that runs out records a code in the device error word,
 // the other roles see it and leave their loops, in-flight copies/MMAs are drained (bounded) and TMEM is freed.
 // No TMA multicast anywhere: each CTA loads its own operand tiles.
@@ -22,11 +25,22 @@ namespace tfb {
 namespace {
 
 constexpr int BM = 128, BN = 256, BKB = 128;  // tile rows, tile cols, K bytes per stage (and swizzle span)
-constexpr int STAGES = 4;
+// Pipeline depth per mode: an NVFP4 stage (operands 48 KB + scales 6 KB) fits 3 times beside the 32 KB epilogue
+// staging, an FP8 stage (48 KB) 4 times.
+template <int MODE>
+struct Stages {
+  static constexpr int value = MODE == 1 ? 4 : 3;
+};
+#ifndef TFB_SF_FROM_GLOBAL
+#define TFB_SF_FROM_GLOBAL 0
+#endif
+constexpr bool SF_GLOBAL = TFB_SF_FROM_GLOBAL;  // scale warps read scales from global (else from the stage's smem)
 constexpr int A_BYTES = BM * BKB;             // 16 KB
 constexpr int B_BYTES = BN * BKB;             // 32 KB
 constexpr int SFA_BYTES = 4 * 512;            // 4 scale chunks (64 K-elements each) of 128 rows
 constexpr int SFB_BYTES = 2 * 4 * 512;        // two 128-row groups
+constexpr int OUT_WARP_BYTES = 32 * 128;      // epilogue staging per warp: 32 rows x 128 B (one TMA store box)
+constexpr int OUT_BYTES = 8 * OUT_WARP_BYTES; // 8 epilogue warps
 constexpr int THREADS = 448;
 constexpr int EPI_WARP0 = 6, SF_WARP0 = 2;
 constexpr uint32_t TMEM_COLS = 512;
@@ -241,27 +255,57 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Two 16-column pieces of this thread's TMEM lane (at taddr_a and taddr_b) with one wait.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t taddr_a, uint32_t taddr_b, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%32];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%33];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr_a), "r"(taddr_b)
+      : "memory");
+}
+
+// TMA tensor store of a 2-D box from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // silu(g) = g / (1 + e^-g) with the hardware exp2 and reciprocal approximations (the reference's Triton kernel
 // used approximate math too); the result is rounded to bf16 by the caller.
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 __host__ __device__ constexpr int smem_bytes(int mode) {
-  return 1024 /* alignment slack */ + STAGES * (A_BYTES + B_BYTES) +
-         (mode == MODE_FP8 ? 0 : STAGES * (SFA_BYTES + SFB_BYTES)) + 256 /* barriers + TMEM slot */;
+  return 1024 /* alignment slack */ + (mode == MODE_FP8 ? 4 : 3) * (A_BYTES + B_BYTES) +
+         (mode == MODE_FP8 || SF_GLOBAL ? 0 : 3 * (SFA_BYTES + SFB_BYTES)) + OUT_BYTES + 256 /* barriers + TMEM */;
 }
 
 // --------------------------------------------------------------------------------------------------- the kernel
 template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmY, const Params p) {
   constexpr bool FP4 = MODE != MODE_FP8;
+  constexpr int STAGES = Stages<MODE>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * A_BYTES;
+  constexpr bool SF_SMEM = FP4 && !SF_GLOBAL;
   uint8_t* sSFA = sB + STAGES * B_BYTES;
-  uint8_t* sSFB = sSFA + (FP4 ? STAGES * SFA_BYTES : 0);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + (FP4 ? STAGES * SFB_BYTES : 0));
+  uint8_t* sSFB = sSFA + (SF_SMEM ? STAGES * SFA_BYTES : 0);
+  uint8_t* sOut = sSFB + (SF_SMEM ? STAGES * SFB_BYTES : 0);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + OUT_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* sf_full = empty + STAGES;
   uint64_t* acc_full = sf_full + STAGES;
@@ -312,24 +356,22 @@ __global__ void __launch_bounds__(THREADS, 1)
           rb0 = nb * BN;
           rb1 = nb * BN + 128;
         }
-        const int g0 = rb0 >> 7, g1 = rb1 >> 7;
         for (int ks = 0; ks < p.num_ks; ++ks) {
           if (!mbar_wait<false>(empty + stage, ph ^ 1, p.err, 0x101)) {
             ok = false;
             break;
           }
-          uint32_t tx = A_BYTES + B_BYTES;
-          uint32_t sf_bytes = 0;
-          if (FP4) {
-            const int kb_here = min(4, p.kb_total - ks * 4);
-            sf_bytes = kb_here * 512;
+          uint32_t tx = A_BYTES + B_BYTES, sf_bytes = 0;
+          const int g0 = rb0 >> 7, g1 = rb1 >> 7;
+          if (SF_SMEM) {
+            sf_bytes = min(4, p.kb_total - ks * 4) * 512;
             tx += sf_bytes * (1 + (g0 < p.sfb_groups) + (g1 < p.sfb_groups));
           }
           mbar_expect_tx(full + stage, tx);
           tma_load_2d(sA + stage * A_BYTES, &tmA, full + stage, ks * BKB, mb * BM);
           tma_load_2d(sB + stage * B_BYTES, &tmB, full + stage, ks * BKB, rb0);
           tma_load_2d(sB + stage * B_BYTES + 128 * BKB, &tmB, full + stage, ks * BKB, rb1);
-          if (FP4) {
+          if (SF_SMEM) {
             const size_t chunk = (size_t)ks * 4;
             bulk_load(sSFA + stage * SFA_BYTES, p.sfa + ((size_t)mb * p.sf_chunks + chunk) * 512, sf_bytes,
                       full + stage);
@@ -364,88 +406,63 @@ __global__ void __launch_bounds__(THREADS, 1)
       // Kept lean: between the last MMA of a stage and the first of the next the thread has about one MMA's
       // execution time (~128 cycles) before the tensor core idles, so descriptors and TMEM addresses are
       // precomputed and both barrier probes of a stage go out in one asm statement.
-      // Everything per stage slot is precomputed; the K loop runs in whole turns of the STAGES-slot ring with the
-      // slot index a compile-time constant, so a stage costs two barrier probes and one asm statement.
-      uint64_t dA[STAGES], dB[STAGES];
-      uint32_t fb[STAGES], sb[STAGES], eb[STAGES], sft[STAGES];
-#pragma unroll
-      for (int s = 0; s < STAGES; ++s) {
-        dA[s] = desc_sw128(sA + s * A_BYTES);
-        dB[s] = desc_sw128(sB + s * B_BYTES);
-        fb[s] = smem_u32(full + s);
-        sb[s] = smem_u32(sf_full + s);
-        eb[s] = smem_u32(empty + s);
-        sft[s] = tmem + SF_COL + s * SF_STAGE_COLS;
-      }
+      // Lean on purpose: the tensor core's MMA queue is ~2 instructions deep, so every cycle the issuing thread
+      // spends between stages is at risk of idling it. Descriptors advance arithmetically (start address >> 4).
+      const uint64_t dA0 = desc_sw128(sA), dB0 = desc_sw128(sB);
+      const uint32_t full0 = smem_u32(full), sf0 = smem_u32(sf_full), empty0 = smem_u32(empty);
       const uint32_t dacc = tmem + ACC_COL;
-      int stage = 0;                           // ring slot of the next stage (tiles need not start at slot 0)
+      int stage = 0;
       uint32_t ph = 0, acc_ph = 0;
       bool ok = true;
-      auto stage_ready = [&](int s, uint32_t par) -> bool {
-        uint32_t r;
-        if (FP4) {
-          asm volatile(
-              "{\n\t.reg .pred p, q;\n\t"
-              "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %3;\n\t"
-              "mbarrier.test_wait.parity.shared::cta.b64 q, [%2], %3;\n\t"
-              "and.pred p, p, q;\n\t"
-              "selp.u32 %0, 1, 0, p;\n\t}"
-              : "=r"(r)
-              : "r"(fb[s]), "r"(sb[s]), "r"(par)
-              : "memory");
-        } else {
-          r = mbar_test(fb[s], par);
-        }
-        if (r) return true;
-        return mbar_wait_slow<true>(fb[s], par, p.err, 0x202) &&
-               (!FP4 || mbar_wait_slow<true>(sb[s], par, p.err, 0x203));
-      };
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         if (!mbar_wait<true>(acc_empty, acc_ph ^ 1, p.err, 0x201)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        int ks = 0;
-        const int full_stages = p.kb_total >> 2;           // stages with all 4 MMA k-blocks
-        // align to the ring so that the unrolled turns below start at slot 0
-        while (ok && stage != 0 && ks < full_stages) {
-          if (!stage_ready(stage, ph)) { ok = false; break; }
-          if (FP4) stage4_fp4(dacc, dA[stage], dB[stage], sft[stage], ks != 0, eb[stage]);
-          else stage4_fp8(dacc, dA[stage], dB[stage], ks != 0, eb[stage]);
-          ++ks;
-          if (++stage == STAGES) { stage = 0; ph ^= 1; }
-        }
-        while (ok && ks + STAGES <= full_stages) {
-#pragma unroll
-          for (int s = 0; s < STAGES; ++s) {
-            if (!stage_ready(s, ph)) { ok = false; break; }
-            if (FP4) stage4_fp4(dacc, dA[s], dB[s], sft[s], (ks + s) != 0, eb[s]);
-            else stage4_fp8(dacc, dA[s], dB[s], (ks + s) != 0, eb[s]);
+        for (int ks = 0; ks < p.num_ks; ++ks) {
+          const uint32_t fbar = full0 + stage * 8, sbar = sf0 + stage * 8;
+          uint32_t ready;
+          if (FP4) {
+            asm volatile(
+                "{\n\t.reg .pred p, q;\n\t"
+                "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %3;\n\t"
+                "mbarrier.test_wait.parity.shared::cta.b64 q, [%2], %3;\n\t"
+                "and.pred p, p, q;\n\t"
+                "selp.u32 %0, 1, 0, p;\n\t}"
+                : "=r"(ready)
+                : "r"(fbar), "r"(sbar), "r"(ph)
+                : "memory");
+          } else {
+            ready = mbar_test(fbar, ph);
           }
-          ks += STAGES;
-          ph ^= 1;
-        }
-        while (ok && ks < p.num_ks) {                     // the remaining stages (and a partial last one)
-          if (!stage_ready(stage, ph)) { ok = false; break; }
+          if (!ready && (!mbar_wait_slow<true>(fbar, ph, p.err, 0x202) ||
+                         (FP4 && !mbar_wait_slow<true>(sbar, ph, p.err, 0x203)))) {
+            ok = false;
+            break;
+          }
+          const uint64_t da = dA0 + (uint64_t)(stage * (A_BYTES >> 4));
+          const uint64_t db = dB0 + (uint64_t)(stage * (B_BYTES >> 4));
+          const uint32_t sft = tmem + SF_COL + stage * SF_STAGE_COLS;
           const int kb_here = min(4, p.kb_total - ks * 4);
           if (kb_here == 4) {
-            if (FP4) stage4_fp4(dacc, dA[stage], dB[stage], sft[stage], ks != 0, eb[stage]);
-            else stage4_fp8(dacc, dA[stage], dB[stage], ks != 0, eb[stage]);
+            if (FP4) stage4_fp4(dacc, da, db, sft, ks != 0, empty0 + stage * 8);
+            else stage4_fp8(dacc, da, db, ks != 0, empty0 + stage * 8);
           } else {
             tc_fence_after();
             for (int kb = 0; kb < kb_here; ++kb) {
               const uint32_t acc = (ks | kb) != 0;
               if (FP4)
-                mma_fp4(dacc, dA[stage] + 2 * kb, dB[stage] + 2 * kb, sft[stage] + kb * 4, sft[stage] + 16 + kb * 8,
-                        acc);
+                mma_fp4(dacc, da + 2 * kb, db + 2 * kb, sft + kb * 4, sft + 16 + kb * 8, acc);
               else
-                mma_fp8(dacc, dA[stage] + 2 * kb, dB[stage] + 2 * kb, acc);
+                mma_fp8(dacc, da + 2 * kb, db + 2 * kb, acc);
             }
             tc_commit(empty + stage);
           }
-          ++ks;
-          if (++stage == STAGES) { stage = 0; ph ^= 1; }
+          if (++stage == STAGES) {
+            stage = 0;
+            ph ^= 1;
+          }
         }
         if (!ok) break;
         tc_commit(acc_full);
@@ -462,26 +479,63 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------------------------------------ scale writers
     // Lane r of quadrant q writes TMEM lane 32q + r: for SFA the 16 bytes at r * 16 of each 512-byte chunk (rows
     // r, r+32, r+64, r+96 x 4 scales), for SFB the same from the two 128-row groups (8 columns). Every quadrant
-    // holds the same values: the block-scaled MMA reads the copy of its own lane quadrant.
+    // holds the same values: the block-scaled MMA reads the copy of its own lane quadrant. The bytes come straight
+    // from global memory (L2-resident scale arrays), so the stage's smem holds only the operand tiles.
     if (FP4) {
       const uint32_t q = warp & 3;
       const uint32_t tq = tmem + ((q * 32) << 16);
       int stage = 0;
       uint32_t ph = 0;
-      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-        bool ok = true;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const int mb = tile % p.num_m, nb = tile / p.num_m;
+        const int g0 = MODE == MODE_FP4_SWIGLU ? nb : 2 * nb;
+        const int g1 = MODE == MODE_FP4_SWIGLU ? (p.N >> 7) + nb : 2 * nb + 1;
+        const uint4* pa = reinterpret_cast<const uint4*>(p.sfa + (size_t)mb * p.sf_chunks * 512) + lane;
+        const uint4* pb0 = reinterpret_cast<const uint4*>(p.sfb + (size_t)g0 * p.sf_chunks * 512) + lane;
+        const uint4* pb1 = reinterpret_cast<const uint4*>(p.sfb + (size_t)g1 * p.sf_chunks * 512) + lane;
+        const bool has_g0 = g0 < p.sfb_groups, has_g1 = g1 < p.sfb_groups;
         for (int ks = 0; ks < p.num_ks; ++ks) {
-          if (!mbar_wait<false>(full + stage, ph, p.err, 0x401)) {
-            ok = false;
-            break;
-          }
           const int kb_here = min(4, p.kb_total - ks * 4);
-          const uint4* a4 = reinterpret_cast<const uint4*>(sSFA + stage * SFA_BYTES) + lane;
-          const uint4* b4 = reinterpret_cast<const uint4*>(sSFB + stage * SFB_BYTES) + lane;
+          uint4 va[4], vb0[4], vb1[4];
+          if (SF_GLOBAL) {
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb) {     // loads first: their latency overlaps the wait below
+              const int c = (ks * 4 + kb) * 32;
+              const bool in = kb < kb_here;
+              va[kb] = in ? __ldg(pa + c) : make_uint4(0, 0, 0, 0);
+              vb0[kb] = in && has_g0 ? __ldg(pb0 + c) : make_uint4(0, 0, 0, 0);
+              vb1[kb] = in && has_g1 ? __ldg(pb1 + c) : make_uint4(0, 0, 0, 0);
+            }
+            // the stage's TMEM scale buffer is free once the MMAs of its previous use completed
+            if (!mbar_wait<false>(empty + stage, ph ^ 1, p.err, 0x401)) {
+              ok = false;
+              break;
+            }
+          } else {
+            // the stage's scales landed in smem (and its TMEM buffer's previous MMAs are done: the producer
+            // re-armed the stage only after they completed)
+            if (!mbar_wait<false>(full + stage, ph, p.err, 0x401)) {
+              ok = false;
+              break;
+            }
+            const uint4* a4 = reinterpret_cast<const uint4*>(sSFA + stage * SFA_BYTES) + lane;
+            const uint4* b4 = reinterpret_cast<const uint4*>(sSFB + stage * SFB_BYTES) + lane;
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb) {
+              va[kb] = a4[kb * 32];
+              vb0[kb] = b4[kb * 32];
+              vb1[kb] = b4[128 + kb * 32];
+            }
+          }
+          tc_fence_after();
           const uint32_t col = SF_COL + stage * SF_STAGE_COLS;
-          for (int kb = 0; kb < kb_here; ++kb) {
-            tmem_st4(tq + col + kb * 4, a4[kb * 32]);
-            tmem_st8(tq + col + 16 + kb * 8, b4[kb * 32], b4[128 + kb * 32]);
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb) {
+            if (kb < kb_here) {
+              tmem_st4(tq + col + kb * 4, va[kb]);
+              tmem_st8(tq + col + 16 + kb * 8, vb0[kb], vb1[kb]);
+            }
           }
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
           tc_fence_before();
@@ -492,7 +546,6 @@ __global__ void __launch_bounds__(THREADS, 1)
             ph ^= 1;
           }
         }
-        if (!ok) break;
       }
     }
   } else {
@@ -501,6 +554,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int half = (warp - EPI_WARP0) >> 2;      // which half of the tile's columns this warp drains
     const int r = q * 32 + lane;                   // row inside the tile == TMEM lane
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+    uint8_t* stg = sOut + (warp - EPI_WARP0) * OUT_WARP_BYTES;   // this warp's 32 x 128-byte staging box
     uint32_t acc_ph = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       if (!mbar_wait<false>(acc_full, acc_ph, p.err, 0x301)) break;
@@ -514,33 +568,31 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t hp[32];                           // 64 bf16 h values, packed in pairs
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          float g[16], u[16];
-          tmem_ld16(trow + ACC_COL + half * 64 + c * 16, g);
-          tmem_ld16(trow + ACC_COL + 128 + half * 64 + c * 16, u);
+          uint32_t raw[32];                        // [0, 16): gate, [16, 32): up -- 16 hidden columns
+          tmem_ld16x2(trow + ACC_COL + half * 64 + c * 16, trow + ACC_COL + 128 + half * 64 + c * 16, raw);
 #pragma unroll
           for (int j = 0; j < 16; j += 2) {
-            const float g0 = bf16_round(g[j] * p.alpha), g1 = bf16_round(g[j + 1] * p.alpha);
-            const float u0 = bf16_round(u[j] * p.alpha), u1 = bf16_round(u[j + 1] * p.alpha);
-            g[j] = g0;
-            g[j + 1] = g1;
-            u[j] = u0;
-            u[j + 1] = u1;
+            const float g0 = bf16_round(__uint_as_float(raw[j]) * p.alpha);
+            const float g1 = bf16_round(__uint_as_float(raw[j + 1]) * p.alpha);
+            const float u0 = bf16_round(__uint_as_float(raw[16 + j]) * p.alpha);
+            const float u1 = bf16_round(__uint_as_float(raw[16 + j + 1]) * p.alpha);
             hp[c * 8 + j / 2] = pack_bf16x2(bf16_round(silu_fast(g0)) * u0, bf16_round(silu_fast(g1)) * u1);
           }
-          if (p.gu_out && m < p.M) {
-            uint4* dg = reinterpret_cast<uint4*>(p.gu_out + m * 2 * F + col0 + c * 16);
-            uint4* du = reinterpret_cast<uint4*>(p.gu_out + m * 2 * F + F + col0 + c * 16);
+          if (p.gu_out && m < p.M) {              // test-only output: the bf16 gate/up values the math used
+            __nv_bfloat16* dg = p.gu_out + m * 2 * F + col0 + c * 16;
 #pragma unroll
-            for (int v = 0; v < 2; ++v) {
-              dg[v] = make_uint4(pack_bf16x2(g[8 * v], g[8 * v + 1]), pack_bf16x2(g[8 * v + 2], g[8 * v + 3]),
-                                 pack_bf16x2(g[8 * v + 4], g[8 * v + 5]), pack_bf16x2(g[8 * v + 6], g[8 * v + 7]));
-              du[v] = make_uint4(pack_bf16x2(u[8 * v], u[8 * v + 1]), pack_bf16x2(u[8 * v + 2], u[8 * v + 3]),
-                                 pack_bf16x2(u[8 * v + 4], u[8 * v + 5]), pack_bf16x2(u[8 * v + 6], u[8 * v + 7]));
+            for (int j = 0; j < 16; j += 2) {
+              *reinterpret_cast<uint32_t*>(dg + j) =
+                  pack_bf16x2(__uint_as_float(raw[j]) * p.alpha, __uint_as_float(raw[j + 1]) * p.alpha);
+              *reinterpret_cast<uint32_t*>(dg + F + j) =
+                  pack_bf16x2(__uint_as_float(raw[16 + j]) * p.alpha, __uint_as_float(raw[16 + j + 1]) * p.alpha);
             }
           }
         }
         tc_fence_before();
         mbar_arrive(acc_empty);                    // accumulator drained: the next tile's MMAs may start
+        if (lane == 0) tma_store_wait_read();      // the staging box is free once the previous store read it
+        __syncwarp();
         if (m < p.M) {
           if (p.h_out) {
             uint4* dh = reinterpret_cast<uint4*>(p.h_out + m * F + col0);
@@ -566,53 +618,64 @@ __global__ void __launch_bounds__(THREADS, 1)
             cw[2 * blk + 1] = nvfp4_codes8(h + 8, inv);
             sfw |= sf << (8 * blk);
           }
-          uint4* dc = reinterpret_cast<uint4*>(p.h_codes + m * (F / 2) + col0 / 2);
+          uint4* dc = reinterpret_cast<uint4*>(stg + lane * 32);
           dc[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
           dc[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
           *reinterpret_cast<uint32_t*>(p.h_sf + sf_tiled_offset(m, col0 / 16, F / 64)) = sfw;
         } else {
           *reinterpret_cast<uint32_t*>(p.h_sf + sf_tiled_offset(m, col0 / 16, F / 64)) = 0u;
         }
+        // 32 rows x 32 bytes of codes for this warp (rows past M are clipped by the tensor map)
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0 && mb * BM + q * 32 < p.M) tma_store_2d(&tmY, stg, (int)(col0 / 2), mb * BM + q * 32);
       } else {
-        // this warp: output columns [half*128, half*128 + 128) of the tile
+        // this warp: output columns [half*128, half*128 + 128) of the tile, drained 64 at a time
         float scale = p.alpha;
         if (MODE == MODE_FP8) scale = __ldg(p.a_scale) * (p.b_per_channel ? 1.0f : __ldg(p.b_scale));
-        const int64_t n_base = (int64_t)nb * BN + half * 128;
+        const int n_base = nb * BN + half * 128;
         uint32_t pk[64];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float v[16];
-          tmem_ld16(trow + ACC_COL + half * 128 + c * 16, v);
-          const int64_t n0 = n_base + c * 16;
-          if (MODE == MODE_FP8 && p.b_per_channel) {
-            const bool inb = n0 < p.N;
+        for (int c = 0; c < 4; ++c) {
+          uint32_t raw[32];
+          tmem_ld16x2(trow + ACC_COL + half * 128 + c * 32, trow + ACC_COL + half * 128 + c * 32 + 16, raw);
+          const int n0 = n_base + c * 32;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] *= scale * (inb ? __ldg(p.b_scale + n0 + j) : 0.0f);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] *= scale;
+          for (int j = 0; j < 16; ++j) {
+            float v0 = __uint_as_float(raw[2 * j]), v1 = __uint_as_float(raw[2 * j + 1]);
+            if (MODE == MODE_FP8 && p.b_per_channel) {
+              const bool inb = n0 + 2 * j < p.N;
+              v0 *= scale * (inb ? __ldg(p.b_scale + n0 + 2 * j) : 0.0f);
+              v1 *= scale * (inb ? __ldg(p.b_scale + n0 + 2 * j + 1) : 0.0f);
+            } else {
+              v0 *= scale;
+              v1 *= scale;
+            }
+            pk[c * 16 + j] = pack_bf16x2(v0, v1);
           }
-#pragma unroll
-          for (int j = 0; j < 8; ++j) pk[c * 8 + j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
         }
         tc_fence_before();
         mbar_arrive(acc_empty);                    // accumulator drained: the next tile's MMAs may start
-        if (m < p.M) {
+        // two 64-column boxes through the 128-byte-swizzled staging buffer and TMA stores (coalesced, async,
+        // clipped at the M / N edges); the buffer is reused once the previous store has read it
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int64_t n0 = n_base + c * 32;
-            if (n0 < p.N) {
-              uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.y) + m * p.ldy + n0);
+        for (int c = 0; c < 2; ++c) {
+          if (lane == 0) tma_store_wait_read();
+          __syncwarp();
 #pragma unroll
-              for (int t = 0; t < 4; ++t)
-                dst[t] = make_uint4(pk[c * 16 + 4 * t], pk[c * 16 + 4 * t + 1], pk[c * 16 + 4 * t + 2],
-                                    pk[c * 16 + 4 * t + 3]);
-            }
-          }
+          for (int ch = 0; ch < 8; ++ch)
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
+                make_uint4(pk[c * 32 + 4 * ch], pk[c * 32 + 4 * ch + 1], pk[c * 32 + 4 * ch + 2],
+                           pk[c * 32 + 4 * ch + 3]);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0 && n_base + c * 64 < p.N && mb * BM + q * 32 < p.M)
+            tma_store_2d(&tmY, stg, n_base + c * 64, mb * BM + q * 32);
         }
       }
       acc_ph ^= 1;
     }
+    if (lane == 0) tma_store_wait_all();
   }
 
   tc_fence_before();
@@ -625,7 +688,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 template <int MODE>
-tfb_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t s) {
+tfb_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty, const Params& p,
+                  cudaStream_t s) {
   const DeviceInfo* di;
   tfb_status st = device_info(&di);
   if (st != TFB_OK) return st;
@@ -636,7 +700,7 @@ tfb_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
   }
   const int grid = p.num_tiles < di->sm_count ? p.num_tiles : di->sm_count;
   if (grid == 0) return TFB_OK;
-  gemm_kernel<MODE><<<grid, THREADS, smem_bytes(MODE), s>>>(ta, tb, p);
+  gemm_kernel<MODE><<<grid, THREADS, smem_bytes(MODE), s>>>(ta, tb, ty, p);
   TFB_CUDA(cudaGetLastError());
   return TFB_OK;
 }
@@ -670,6 +734,8 @@ tfb_status gemm_nvfp4(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, c
   CUtensorMap ta, tb;
   if ((st = make_tmap_u8(&ta, a, K / 2, M, K / 2, BKB, BM)) != TFB_OK) return st;
   if ((st = make_tmap_u8(&tb, b, K / 2, N, K / 2, BKB, 128)) != TFB_OK) return st;
+  CUtensorMap ty;
+  if ((st = make_tmap_2d(&ty, y, 2, N, M, ldy * 2, 64, 32, true)) != TFB_OK) return st;
   Params p{};
   p.M = (int)M;
   p.N = (int)N;
@@ -685,7 +751,7 @@ tfb_status gemm_nvfp4(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, c
   p.ldy = ldy;
   p.alpha = alpha;
   p.err = di->err_word;
-  return launch<MODE_FP4>(ta, tb, p, s);
+  return launch<MODE_FP4>(ta, tb, ty, p, s);
 }
 
 tfb_status gemm_nvfp4_swiglu(const uint8_t* a, const uint8_t* a_sf, const uint8_t* gu, const uint8_t* gu_sf, int64_t M,
@@ -722,7 +788,9 @@ tfb_status gemm_nvfp4_swiglu(const uint8_t* a, const uint8_t* a_sf, const uint8_
   p.gu_out = static_cast<__nv_bfloat16*>(gu_out);
   p.h_out = static_cast<__nv_bfloat16*>(h_out);
   p.err = di->err_word;
-  return launch<MODE_FP4_SWIGLU>(ta, tb, p, s);
+  CUtensorMap th;                                      // h codes: 32-byte x 32-row boxes, one per epilogue warp
+  if ((st = make_tmap_2d(&th, h_codes, 1, F / 2, M, F / 2, 32, 32, false)) != TFB_OK) return st;
+  return launch<MODE_FP4_SWIGLU>(ta, tb, th, p, s);
 }
 
 tfb_status gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, int64_t K, const float* a_scale,
@@ -737,6 +805,8 @@ tfb_status gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, in
   CUtensorMap ta, tb;
   if ((st = make_tmap_u8(&ta, a, K, M, K, BKB, BM)) != TFB_OK) return st;
   if ((st = make_tmap_u8(&tb, b, K, N, K, BKB, 128)) != TFB_OK) return st;
+  CUtensorMap ty;
+  if ((st = make_tmap_2d(&ty, y, 2, N, M, ldy * 2, 64, 32, true)) != TFB_OK) return st;
   Params p{};
   p.M = (int)M;
   p.N = (int)N;
@@ -750,7 +820,7 @@ tfb_status gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, in
   p.b_scale = b_scale;
   p.b_per_channel = per_channel;
   p.err = di->err_word;
-  return launch<MODE_FP8>(ta, tb, p, s);
+  return launch<MODE_FP8>(ta, tb, ty, p, s);
 }
 
 }  // namespace tfb

@@ -60,8 +60,8 @@ tfb_status device_info(const DeviceInfo** out) {
   return TFB_OK;
 }
 
-tfb_status make_tmap_u8(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint64_t row_stride,
-                        uint32_t box_inner, uint32_t box_rows) {
+tfb_status make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t rows,
+                        uint64_t row_stride, uint32_t box_inner, uint32_t box_rows, bool swizzle) {
   if (!g_encode) {
     std::lock_guard<std::mutex> lock(g_dev_mu);
     if (!g_encode) {
@@ -75,15 +75,22 @@ tfb_status make_tmap_u8(CUtensorMap* map, const void* base, uint64_t inner_bytes
   if (!aligned(base, 16) || row_stride % 16 != 0)
     return fail(TFB_BAD_ALIGN, "TMA operand needs a 16-byte aligned base and row stride (stride %llu)",
                 (unsigned long long)row_stride);
-  cuuint64_t dims[2] = {inner_bytes, rows};
+  cuuint64_t dims[2] = {inner, rows};
   cuuint64_t strides[1] = {row_stride};
   cuuint32_t box[2] = {box_inner, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  const CUtensorMapDataType dt = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TFB_CUDA_ERR, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
   return TFB_OK;
+}
+
+tfb_status make_tmap_u8(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint64_t row_stride,
+                        uint32_t box_inner, uint32_t box_rows) {
+  return make_tmap_2d(map, base, 1, inner_bytes, rows, row_stride, box_inner, box_rows, true);
 }
 
 }  // namespace tfb

@@ -34,6 +34,9 @@ inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintp
 // box `box_inner` x `box_rows`, 128-byte swizzle, zero fill out of bounds.
 tfb_status make_tmap_u8(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint64_t row_stride,
                         uint32_t box_inner, uint32_t box_rows);
+// Same for 1- or 2-byte elements: `inner` elements per row, box `box_inner` elements, 128-byte swizzle or none.
+tfb_status make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t rows,
+                        uint64_t row_stride, uint32_t box_inner, uint32_t box_rows, bool swizzle);
 
 // NVFP4 row quantizer launch (quant.cu); shared by the fused MLP entry point.
 tfb_status quant_nvfp4(const void* x, int64_t M, int64_t K, int64_t ldx, float g, uint8_t* codes, uint8_t* sf,
