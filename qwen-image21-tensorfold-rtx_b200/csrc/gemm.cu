@@ -1,42 +1,40 @@
 // tcgen05 GEMMs for sm_100a: NVFP4 W4A4 (kind::mxf4nvf4, E4M3 block scales per 16), FP8 W8A8 (kind::f8f6f4), and
 // the NVFP4 gate/up GEMM whose epilogue applies SwiGLU and writes NVFP4 rows + scales for the down projection.
 //
-// One persistent CTA per SM walks 128 x 256 output tiles (M fastest). Warp roles (448 threads, 14 warps):
-//   warp 0 lane 0 : TMA producer -- per stage an A tile [128 rows x 128 B] and a B tile [256 rows x 128 B] (two
-//                   128-row boxes), 128-byte swizzle.
-//   warp 1        : allocates TMEM (512 columns); lane 0 issues tcgen05.mma (M=128, N=256, K=64 fp4 / 32 fp8) into
-//                   a 256-column fp32 accumulator. Its waits poll with mbarrier.test_wait: a blocking try_wait on
-//                   the issue path costs ~128 cycles per stage, a quarter of the stage's MMA time.
-//   warps 2..5    : scale writers (NVFP4 modes) -- load the stage's scales from global memory into registers and
-//                   write them to TMEM with tcgen05.st (one warp per TMEM lane quadrant). tcgen05.cp of the same
-//                   bytes serialises with the MMAs and costs ~40% of the tensor time; tcgen05.st from four warps
-//                   runs alongside them.
+// Persistent kernel, one CTA per SM. For M > 128 the CTAs work in pairs (a 2-CTA cluster, tcgen05 cta_group::2):
+// the pair owns a 256 x 256 output tile, each CTA holds 128 A rows and half of the tile's 256 B rows in its shared
+// memory, and the leader (rank 0) issues M=256 MMAs that run on both SMs' tensor cores, each accumulating its own
+// 128 rows x 256 columns in its own TMEM. Per SM that halves the B bytes TMA must deliver per MMA (the single-CTA
+// kernel was bound by it). M <= 128 uses single CTAs on 128 x 256 tiles. Warp roles (448 threads, 14 warps):
+//   warp 0 lane 0 : TMA producer -- per stage its A tile [128 rows x 128 B] and B rows [128 (pair) or 256 x 128 B],
+//                   128-byte swizzle, plus the stage's scale chunks (NVFP4). In a pair the tile loads of both CTAs
+//                   complete on the leader's `full` barrier (cta_group::2 tensor loads), so the MMA thread waits
+//                   on one local barrier for both halves.
+//   warp 1        : allocates TMEM (512 columns); lane 0 of the leader issues tcgen05.mma (N=256, K=64 fp4 / 32
+//                   fp8) into a 256-column fp32 accumulator. Its waits poll with mbarrier.test_wait: a blocking
+//                   try_wait on the issue path costs ~128 cycles per stage, a quarter of the stage's MMA time.
+//   warps 2..5    : scale writers (NVFP4 modes) -- copy the stage's scales from shared memory into this CTA's TMEM
+//                   with tcgen05.st (one warp per TMEM lane quadrant) and arrive on the leader's `ready` barrier.
+//                   tcgen05.cp of the same bytes serialises with the MMAs and costs ~40% of the tensor time;
+//                   tcgen05.st from four warps runs alongside them.
 //   warps 6..13   : epilogue, two warps per TMEM lane quadrant (warp w reads lanes 32*(w%4)..+31, one output row
 //                   per thread, each warp half of the columns). They drain the accumulator into registers, release
-//                   it to the MMA warp, then scale / convert / store while the next tile's MMAs run. bf16 outputs
+//                   it to the MMA thread, then scale / convert / store while the next tile's MMAs run. bf16 outputs
 //                   go through a 128-byte-swizzled smem box per warp and TMA tensor stores: per-row 16-byte global
 //                   stores crowd the memory-instruction path the MMA issue shares and stalled it ~4500 cycles/tile.
 // Every mbarrier wait is bounded (kWaitLimitNs); a wait that runs out records a code in the device error word,
 // the other roles see it and leave their loops, in-flight copies/MMAs are drained (bounded) and TMEM is freed.
 // No TMA multicast anywhere: each CTA loads its own operand tiles.
+#include <stdlib.h>
+
 #include "tfb_common.cuh"
 
 namespace tfb {
 namespace {
 
 constexpr int BM = 128, BN = 256, BKB = 128;  // tile rows, tile cols, K bytes per stage (and swizzle span)
-// Pipeline depth per mode: an NVFP4 stage (operands 48 KB + scales 6 KB) fits 3 times beside the 32 KB epilogue
-// staging, an FP8 stage (48 KB) 4 times.
-template <int MODE>
-struct Stages {
-  static constexpr int value = MODE == 1 ? 4 : 3;
-};
-#ifndef TFB_SF_FROM_GLOBAL
-#define TFB_SF_FROM_GLOBAL 0
-#endif
-constexpr bool SF_GLOBAL = TFB_SF_FROM_GLOBAL;  // scale warps read scales from global (else from the stage's smem)
+
 constexpr int A_BYTES = BM * BKB;             // 16 KB
-constexpr int B_BYTES = BN * BKB;             // 32 KB
 constexpr int SFA_BYTES = 4 * 512;            // 4 scale chunks (64 K-elements each) of 128 rows
 constexpr int SFB_BYTES = 2 * 4 * 512;        // two 128-row groups
 constexpr int OUT_WARP_BYTES = 32 * 128;      // epilogue staging per warp: 32 rows x 128 B (one TMA store box)
@@ -60,6 +58,7 @@ struct Params {
   const uint8_t* sfb;
   int sf_chunks;         // K / 64
   int sfb_groups;        // ceil(b_rows / 128)
+  int sfa_groups;        // ceil(M / 128): scale groups (and tiled-scale rows / 128) of A and of the h output
   void* y;
   int64_t ldy;
   float alpha;           // fp4: g_a * g_b
@@ -138,6 +137,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
       : "memory");
 }
+// CTA-pair form: the transaction bytes land on the mbarrier at `bar` (a shared::cluster address, here the leader
+// CTA's), while the data goes to this CTA's shared memory.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
@@ -146,10 +154,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
 
 // Shared-memory matrix descriptor, K-major, 128-byte swizzle: rows 128 B apart, 8-row groups 1024 B apart.
 __device__ __forceinline__ uint64_t desc_sw128(const void* p) {
@@ -157,60 +161,141 @@ __device__ __forceinline__ uint64_t desc_sw128(const void* p) {
   return ((a & 0x3FFFFull) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
 
-// Instruction descriptors (M = 128, N = 256, both operands K-major, fp32 accumulate).
+// Instruction descriptors (M = 128 per CTA of the group, N = 256, both operands K-major, fp32 accumulate).
 //   block-scaled mxf4nvf4: A/B format E2M1 (1) at bits 7-9 / 10-12, scale format UE4M3 (0) at bit 23;
-//   f8f6f4: D format F32 (1) at bits 4-5, A/B format E4M3 (0).
-constexpr uint32_t IDESC_FP4 = (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-constexpr uint32_t IDESC_FP8 = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+//   f8f6f4: D format F32 (1) at bits 4-5, A/B format E4M3 (0). M is encoded >> 4 at bits 24-28, N >> 3 at 17-22.
+template <int CG>
+struct Idesc {
+  static constexpr uint32_t fp4 = (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM * CG >> 4) << 24);
+  static constexpr uint32_t fp8 = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM * CG >> 4) << 24);
+};
 
+template <int CG>
 __device__ __forceinline__ void mma_fp4(uint32_t d, uint64_t a, uint64_t b, uint32_t sfa, uint32_t sfb, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
-      ::"r"(d), "l"(a), "l"(b), "r"(IDESC_FP4), "r"(acc), "r"(sfa), "r"(sfb)
-      : "memory");
+  if (CG == 2)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+        ::"r"(d), "l"(a), "l"(b), "r"(Idesc<2>::fp4), "r"(acc), "r"(sfa), "r"(sfb)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+        ::"r"(d), "l"(a), "l"(b), "r"(Idesc<1>::fp4), "r"(acc), "r"(sfa), "r"(sfb)
+        : "memory");
 }
+template <int CG>
 __device__ __forceinline__ void mma_fp8(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(d), "l"(a), "l"(b), "r"(IDESC_FP8), "r"(acc)
-      : "memory");
+  if (CG == 2)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d), "l"(a), "l"(b), "r"(Idesc<2>::fp8), "r"(acc)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d), "l"(a), "l"(b), "r"(Idesc<1>::fp8), "r"(acc)
+        : "memory");
+}
+// Commit of every tcgen05 op issued so far to an mbarrier at the same smem offset in each CTA of the group
+// (tcgen05.commit multicast to the CTA pair: a signal, not a data load).
+template <int CG>
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  if (CG == 2)
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"((uint16_t)3)
+        : "memory");
+  else
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// Commit to this CTA's barrier only.
+template <int CG>
+__device__ __forceinline__ void tc_commit_local(uint32_t bar) {
+  if (CG == 2)
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+  else
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// Arrive on the leader CTA's mbarrier (a shared::cluster address) from the follower CTA of a pair. Relaxed: what
+// the leader consumes after the wait is never ordinary memory published by this arrive -- it is this CTA's TMEM,
+// whose tcgen05.st / tcgen05.ld traffic has completed (tcgen05.wait::st / ::ld) before the arrive and is ordered
+// around it by tcgen05.fence::before_thread_sync here and ::after_thread_sync on the leader. A release at cluster
+// scope made each arrive take ~0.7 us, which starved the MMA issue of the pair by ~40%.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
 }
 
-// fence::after_thread_sync + 4 MMAs + the commit that frees the stage's smem slot, as one asm statement.
+// fence::after_thread_sync + 4 MMAs + the commit that frees the stage's smem slot(s), as one asm statement.
+template <int CG>
 __device__ __forceinline__ void stage4_fp4(uint32_t d, uint64_t da, uint64_t db, uint32_t sf, uint32_t acc0,
                                            uint32_t empty_bar) {
-  asm volatile(
-      "{\n\t.reg .pred pa;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t.reg .b32 s1, s2, s3, t0, t1, t2, t3;\n\t"
-      "setp.ne.b32 pa, %5, 0;\n\t"
-      "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\t"
-      "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\t"
-      "add.u32 s1, %3, 4;\n\tadd.u32 s2, %3, 8;\n\tadd.u32 s3, %3, 12;\n\t"
-      "add.u32 t0, %3, 16;\n\tadd.u32 t1, %3, 24;\n\tadd.u32 t2, %3, 32;\n\tadd.u32 t3, %3, 40;\n\t"
-      "tcgen05.fence::after_thread_sync;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %6, [%3], [t0], pa;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], a1, b1, %6, [s1], [t1], 1;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], a2, b2, %6, [s2], [t2], 1;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], a3, b3, %6, [s3], [t3], 1;\n\t"
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%4];\n\t}"
-      ::"r"(d), "l"(da), "l"(db), "r"(sf), "r"(empty_bar), "r"(acc0), "r"(IDESC_FP4)
-      : "memory");
+  if (CG == 2)
+    asm volatile(
+        "{\n\t.reg .pred pa;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t.reg .b32 s1, s2, s3, t0, t1, t2, t3;\n\t"
+        "setp.ne.b32 pa, %5, 0;\n\t"
+        "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\t"
+        "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\t"
+        "add.u32 s1, %3, 4;\n\tadd.u32 s2, %3, 8;\n\tadd.u32 s3, %3, 12;\n\t"
+        "add.u32 t0, %3, 16;\n\tadd.u32 t1, %3, 24;\n\tadd.u32 t2, %3, 32;\n\tadd.u32 t3, %3, 40;\n\t"
+        "tcgen05.fence::after_thread_sync;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %6, [%3], [t0], pa;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], a1, b1, %6, [s1], [t1], 1;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], a2, b2, %6, [s2], [t2], 1;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], a3, b3, %6, [s3], [t3], 1;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%4], %7;\n\t}"
+        ::"r"(d), "l"(da), "l"(db), "r"(sf), "r"(empty_bar), "r"(acc0), "r"(Idesc<2>::fp4), "h"((uint16_t)3)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred pa;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t.reg .b32 s1, s2, s3, t0, t1, t2, t3;\n\t"
+        "setp.ne.b32 pa, %5, 0;\n\t"
+        "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\t"
+        "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\t"
+        "add.u32 s1, %3, 4;\n\tadd.u32 s2, %3, 8;\n\tadd.u32 s3, %3, 12;\n\t"
+        "add.u32 t0, %3, 16;\n\tadd.u32 t1, %3, 24;\n\tadd.u32 t2, %3, 32;\n\tadd.u32 t3, %3, 40;\n\t"
+        "tcgen05.fence::after_thread_sync;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %6, [%3], [t0], pa;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], a1, b1, %6, [s1], [t1], 1;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], a2, b2, %6, [s2], [t2], 1;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], a3, b3, %6, [s3], [t3], 1;\n\t"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%4];\n\t}"
+        ::"r"(d), "l"(da), "l"(db), "r"(sf), "r"(empty_bar), "r"(acc0), "r"(Idesc<1>::fp4)
+        : "memory");
 }
+template <int CG>
 __device__ __forceinline__ void stage4_fp8(uint32_t d, uint64_t da, uint64_t db, uint32_t acc0, uint32_t empty_bar) {
-  asm volatile(
-      "{\n\t.reg .pred pa;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
-      "setp.ne.b32 pa, %4, 0;\n\t"
-      "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\t"
-      "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\t"
-      "tcgen05.fence::after_thread_sync;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %5, pa;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], a1, b1, %5, 1;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], a2, b2, %5, 1;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], a3, b3, %5, 1;\n\t"
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%3];\n\t}"
-      ::"r"(d), "l"(da), "l"(db), "r"(empty_bar), "r"(acc0), "r"(IDESC_FP8)
-      : "memory");
+  if (CG == 2)
+    asm volatile(
+        "{\n\t.reg .pred pa;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+        "setp.ne.b32 pa, %4, 0;\n\t"
+        "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\t"
+        "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\t"
+        "tcgen05.fence::after_thread_sync;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %5, pa;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], a1, b1, %5, 1;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], a2, b2, %5, 1;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], a3, b3, %5, 1;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%3], %6;\n\t}"
+        ::"r"(d), "l"(da), "l"(db), "r"(empty_bar), "r"(acc0), "r"(Idesc<2>::fp8), "h"((uint16_t)3)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred pa;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+        "setp.ne.b32 pa, %4, 0;\n\t"
+        "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\t"
+        "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\t"
+        "tcgen05.fence::after_thread_sync;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %5, pa;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], a1, b1, %5, 1;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], a2, b2, %5, 1;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], a3, b3, %5, 1;\n\t"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%3];\n\t}"
+        ::"r"(d), "l"(da), "l"(db), "r"(empty_bar), "r"(acc0), "r"(Idesc<1>::fp8)
+        : "memory");
 }
 
 // Warp-collective TMEM stores of this warp's 32 lanes: 4 and 8 consecutive 32-bit columns.
@@ -285,56 +370,91 @@ __device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bu
 // used approximate math too); the result is rounded to bf16 by the caller.
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
-__host__ __device__ constexpr int smem_bytes(int mode) {
-  return 1024 /* alignment slack */ + (mode == MODE_FP8 ? 4 : 3) * (A_BYTES + B_BYTES) +
-         (mode == MODE_FP8 || SF_GLOBAL ? 0 : 3 * (SFA_BYTES + SFB_BYTES)) + OUT_BYTES + 256 /* barriers + TMEM */;
-}
 
 // --------------------------------------------------------------------------------------------------- the kernel
-template <int MODE>
+// Pipeline depth per (mode, CTA group): an NVFP4 stage holds A 16 KB + B 16 KB per CTA of the group's B half
+// (1 CTA: the whole 32 KB B tile) + 6 KB of scales; FP8 stages have no scales. All fit beside the 32 KB epilogue
+// staging in the 227 KB of shared memory.
+template <int MODE, int CG>
+struct Cfg {
+  static constexpr int B_BYTES_CTA = CG == 2 ? 128 * BKB : BN * BKB;
+  static constexpr int SF_BYTES = MODE == 1 ? 0 : SFA_BYTES + SFB_BYTES;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES_CTA + SF_BYTES;
+  static constexpr int STAGES = CG == 2 ? (MODE == 1 ? 6 : 5) : (MODE == 1 ? 4 : 3);
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + OUT_BYTES + 512;
+};
+
+template <int MODE, int CG>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmY, const Params p) {
+  using C = Cfg<MODE, CG>;
   constexpr bool FP4 = MODE != MODE_FP8;
-  constexpr int STAGES = Stages<MODE>::value;
+  constexpr int STAGES = C::STAGES;
+  constexpr int B_BYTES_CTA = C::B_BYTES_CTA;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * A_BYTES;
-  constexpr bool SF_SMEM = FP4 && !SF_GLOBAL;
-  uint8_t* sSFA = sB + STAGES * B_BYTES;
-  uint8_t* sSFB = sSFA + (SF_SMEM ? STAGES * SFA_BYTES : 0);
-  uint8_t* sOut = sSFB + (SF_SMEM ? STAGES * SFB_BYTES : 0);
+  uint8_t* sSFA = sB + STAGES * B_BYTES_CTA;
+  uint8_t* sSFB = sSFA + (FP4 ? STAGES * SFA_BYTES : 0);
+  uint8_t* sOut = sSFB + (FP4 ? STAGES * SFB_BYTES : 0);
+  // full: the stage's loads landed -- one CTA: all of them; a pair: the leader's copy counts both CTAs' operand
+  // tiles (each CTA's tensor loads complete on it), the follower's is unused
   uint64_t* full = reinterpret_cast<uint64_t*>(sOut + OUT_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* sf_full = empty + STAGES;
-  uint64_t* acc_full = sf_full + STAGES;
-  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* empty = full + STAGES;          // the stage's MMAs completed (commit from the group's MMA thread)
+  uint64_t* ready = empty + STAGES;         // leader: every scale warp of the group finished the stage
+  uint64_t* sff = ready + STAGES;           // a pair: this CTA's scale bytes landed (its scale warps wait here)
+  uint64_t* acc_full = sff + STAGES;
+  uint64_t* acc_empty = acc_full + 1;       // leader: every epilogue warp of the group drained the accumulator
   uint64_t* drain = acc_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t rank = 0;                        // CTA rank inside the MMA group (0 = leader, issues the MMAs)
+  if (CG == 2) asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  const int grp = blockIdx.x / CG, ngrp = gridDim.x / CG;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
-      mbar_init(sf_full + s, 4);   // one arrival per scale warp
+      mbar_init(ready + s, 4 * CG);
+      mbar_init(sff + s, 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 256);     // every epilogue thread
+    mbar_init(acc_empty, 8 * CG);
     mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if (CG == 2) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(TMEM_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(TMEM_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (CG == 2) {
+    // barriers of both CTAs are initialised before either CTA signals the other
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the leader's copies of `ready` and `acc_empty`, as shared::cluster addresses
+  uint32_t ready_l = smem_u32(ready), acc_empty_l = smem_u32(acc_empty), full_l = smem_u32(full);
+  if (CG == 2 && rank != 0) {
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(ready_l) : "r"(ready_l));
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(acc_empty_l) : "r"(acc_empty_l));
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(full_l) : "r"(full_l));
+  }
 
   if (warp == 0) {
     if (lane == 0) {
@@ -346,9 +466,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t issued = 0;     // bit s: stage s was armed at least once
       uint32_t last_ph = 0;    // bit s: parity of its last arming
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+      for (int tile = grp; ok && tile < p.num_tiles; tile += ngrp) {
         const int mb = tile % p.num_m, nb = tile / p.num_m;
-        int rb0, rb1;
+        const int arow = mb * (BM * CG) + (int)rank * BM;             // this CTA's A rows
+        int rb0, rb1;                                                  // the tile's two 128-row B groups
         if (MODE == MODE_FP4_SWIGLU) {
           rb0 = nb * 128;
           rb1 = p.N + nb * 128;
@@ -356,31 +477,41 @@ __global__ void __launch_bounds__(THREADS, 1)
           rb0 = nb * BN;
           rb1 = nb * BN + 128;
         }
+        const int g0 = rb0 >> 7, g1 = rb1 >> 7, ga = arow >> 7;
         for (int ks = 0; ks < p.num_ks; ++ks) {
           if (!mbar_wait<false>(empty + stage, ph ^ 1, p.err, 0x101)) {
             ok = false;
             break;
           }
-          uint32_t tx = A_BYTES + B_BYTES, sf_bytes = 0;
-          const int g0 = rb0 >> 7, g1 = rb1 >> 7;
-          if (SF_SMEM) {
+          uint32_t sf_bytes = 0, sf_tx = 0;
+          if (FP4) {
             sf_bytes = min(4, p.kb_total - ks * 4) * 512;
-            tx += sf_bytes * (1 + (g0 < p.sfb_groups) + (g1 < p.sfb_groups));
+            sf_tx = sf_bytes * ((ga < p.sfa_groups) + (g0 < p.sfb_groups) + (g1 < p.sfb_groups));
           }
-          mbar_expect_tx(full + stage, tx);
-          tma_load_2d(sA + stage * A_BYTES, &tmA, full + stage, ks * BKB, mb * BM);
-          tma_load_2d(sB + stage * B_BYTES, &tmB, full + stage, ks * BKB, rb0);
-          tma_load_2d(sB + stage * B_BYTES + 128 * BKB, &tmB, full + stage, ks * BKB, rb1);
-          if (SF_SMEM) {
+          // scale copies complete on this CTA's own barrier: `full` (one CTA) or `sff` (a pair)
+          uint64_t* sf_bar = CG == 2 ? sff + stage : full + stage;
+          if (CG == 2) {
+            // both CTAs' operand tiles complete on the leader's `full`, which the leader alone arms (tile loads
+            // always count their whole box, rows past the tensor's end included)
+            if (rank == 0) mbar_expect_tx(full + stage, 2 * (A_BYTES + B_BYTES_CTA));
+            if (FP4) mbar_expect_tx(sff + stage, sf_tx);
+            tma_load_2d_pair(sA + stage * A_BYTES, &tmA, full_l + stage * 8, ks * BKB, arow);
+            tma_load_2d_pair(sB + stage * B_BYTES_CTA, &tmB, full_l + stage * 8, ks * BKB, rank == 0 ? rb0 : rb1);
+          } else {
+            mbar_expect_tx(full + stage, A_BYTES + B_BYTES_CTA + sf_tx);
+            tma_load_2d(sA + stage * A_BYTES, &tmA, full + stage, ks * BKB, arow);
+            tma_load_2d(sB + stage * B_BYTES_CTA, &tmB, full + stage, ks * BKB, rb0);
+            tma_load_2d(sB + stage * B_BYTES_CTA + 128 * BKB, &tmB, full + stage, ks * BKB, rb1);
+          }
+          if (FP4) {
             const size_t chunk = (size_t)ks * 4;
-            bulk_load(sSFA + stage * SFA_BYTES, p.sfa + ((size_t)mb * p.sf_chunks + chunk) * 512, sf_bytes,
-                      full + stage);
+            if (ga < p.sfa_groups)
+              bulk_load(sSFA + stage * SFA_BYTES, p.sfa + ((size_t)ga * p.sf_chunks + chunk) * 512, sf_bytes, sf_bar);
             if (g0 < p.sfb_groups)
-              bulk_load(sSFB + stage * SFB_BYTES, p.sfb + ((size_t)g0 * p.sf_chunks + chunk) * 512, sf_bytes,
-                        full + stage);
+              bulk_load(sSFB + stage * SFB_BYTES, p.sfb + ((size_t)g0 * p.sf_chunks + chunk) * 512, sf_bytes, sf_bar);
             if (g1 < p.sfb_groups)
               bulk_load(sSFB + stage * SFB_BYTES + 2048, p.sfb + ((size_t)g1 * p.sf_chunks + chunk) * 512, sf_bytes,
-                        full + stage);
+                        sf_bar);
           }
           issued |= 1u << stage;
           last_ph = (last_ph & ~(1u << stage)) | (ph << stage);
@@ -393,71 +524,94 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!ok) {  // let every copy already in flight land before the CTA exits
         for (int s = 0; s < STAGES; ++s)
           if (issued & (1u << s)) {
-            const uint32_t a = smem_u32(full + s);
-            const unsigned long long t0 = globaltimer();
-            while (!mbar_try(a, (last_ph >> s) & 1) && (long long)(globaltimer() - t0) < kWaitLimitNs) {
+            // one CTA: `full` counts all of its copies; a pair: `sff` this CTA's scale copies and the leader's
+            // `full` both CTAs' tiles (the follower cannot wait on the leader's barrier; it pauses instead, below)
+            for (int b = 0; b < 2; ++b) {
+              const uint64_t* bar = b == 0 ? full + s : sff + s;
+              if ((b == 0 && CG == 2 && rank != 0) || (b == 1 && (CG == 1 || !FP4))) continue;
+              const uint32_t a = smem_u32(bar);
+              const unsigned long long t0 = globaltimer();
+              while (!mbar_try(a, (last_ph >> s) & 1) && (long long)(globaltimer() - t0) < kWaitLimitNs) {
+              }
             }
           }
+        // a pair: tiles this CTA issued for a stage the leader never armed complete on no barrier either CTA
+        // can wait for; a tile load lands within microseconds, so both CTAs stay for 100 us before leaving
+        if (CG == 2) {
+          const unsigned long long t0 = globaltimer();
+          while ((long long)(globaltimer() - t0) < 100000) {
+          }
+        }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       // --------------------------------------------------------------------------------------------- MMA
-      // Kept lean: between the last MMA of a stage and the first of the next the thread has about one MMA's
-      // execution time (~128 cycles) before the tensor core idles, so descriptors and TMEM addresses are
-      // precomputed and both barrier probes of a stage go out in one asm statement.
       // Lean on purpose: the tensor core's MMA queue is ~2 instructions deep, so every cycle the issuing thread
       // spends between stages is at risk of idling it. Descriptors advance arithmetically (start address >> 4).
       const uint64_t dA0 = desc_sw128(sA), dB0 = desc_sw128(sB);
-      const uint32_t full0 = smem_u32(full), sf0 = smem_u32(sf_full), empty0 = smem_u32(empty);
+      const uint32_t full0 = smem_u32(full), rdy0 = smem_u32(ready), empty0 = smem_u32(empty);
       const uint32_t dacc = tmem + ACC_COL;
       int stage = 0;
       uint32_t ph = 0, acc_ph = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+      for (int tile = grp; ok && tile < p.num_tiles; tile += ngrp) {
         if (!mbar_wait<true>(acc_empty, acc_ph ^ 1, p.err, 0x201)) {
           ok = false;
           break;
         }
         tc_fence_after();
         for (int ks = 0; ks < p.num_ks; ++ks) {
-          const uint32_t fbar = full0 + stage * 8, sbar = sf0 + stage * 8;
-          uint32_t ready;
-          if (FP4) {
+          const uint32_t fbar = full0 + stage * 8, rbar = rdy0 + stage * 8;
+          uint32_t go;
+          if (CG == 2 && FP4) {   // both CTAs' tiles (leader's `full`), both CTAs' scales in TMEM (`ready`)
+            asm volatile(
+                "{\n\t.reg .pred p, q;\n\t"
+                "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %3;\n\t"
+                "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 q, [%2], %3;\n\t"
+                "and.pred p, p, q;\n\t"
+                "selp.u32 %0, 1, 0, p;\n\t}"
+                : "=r"(go)
+                : "r"(fbar), "r"(rbar), "r"(ph)
+                : "memory");
+          } else if (FP4) {
             asm volatile(
                 "{\n\t.reg .pred p, q;\n\t"
                 "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %3;\n\t"
                 "mbarrier.test_wait.parity.shared::cta.b64 q, [%2], %3;\n\t"
                 "and.pred p, p, q;\n\t"
                 "selp.u32 %0, 1, 0, p;\n\t}"
-                : "=r"(ready)
-                : "r"(fbar), "r"(sbar), "r"(ph)
+                : "=r"(go)
+                : "r"(fbar), "r"(rbar), "r"(ph)
                 : "memory");
           } else {
-            ready = mbar_test(fbar, ph);
+            go = mbar_test(fbar, ph);
           }
-          if (!ready && (!mbar_wait_slow<true>(fbar, ph, p.err, 0x202) ||
-                         (FP4 && !mbar_wait_slow<true>(sbar, ph, p.err, 0x203)))) {
-            ok = false;
-            break;
+          if (!go) {
+            const bool waited = mbar_wait_slow<true>(fbar, ph, p.err, 0x202) &&
+                                (!FP4 || mbar_wait_slow<true>(rbar, ph, p.err, 0x203));
+            if (!waited) {
+              ok = false;
+              break;
+            }
           }
           const uint64_t da = dA0 + (uint64_t)(stage * (A_BYTES >> 4));
-          const uint64_t db = dB0 + (uint64_t)(stage * (B_BYTES >> 4));
+          const uint64_t db = dB0 + (uint64_t)(stage * (B_BYTES_CTA >> 4));
           const uint32_t sft = tmem + SF_COL + stage * SF_STAGE_COLS;
           const int kb_here = min(4, p.kb_total - ks * 4);
           if (kb_here == 4) {
-            if (FP4) stage4_fp4(dacc, da, db, sft, ks != 0, empty0 + stage * 8);
-            else stage4_fp8(dacc, da, db, ks != 0, empty0 + stage * 8);
+            if (FP4) stage4_fp4<CG>(dacc, da, db, sft, ks != 0, empty0 + stage * 8);
+            else stage4_fp8<CG>(dacc, da, db, ks != 0, empty0 + stage * 8);
           } else {
             tc_fence_after();
             for (int kb = 0; kb < kb_here; ++kb) {
               const uint32_t acc = (ks | kb) != 0;
               if (FP4)
-                mma_fp4(dacc, da + 2 * kb, db + 2 * kb, sft + kb * 4, sft + 16 + kb * 8, acc);
+                mma_fp4<CG>(dacc, da + 2 * kb, db + 2 * kb, sft + kb * 4, sft + 16 + kb * 8, acc);
               else
-                mma_fp8(dacc, da + 2 * kb, db + 2 * kb, acc);
+                mma_fp8<CG>(dacc, da + 2 * kb, db + 2 * kb, acc);
             }
-            tc_commit(empty + stage);
+            tc_commit<CG>(empty0 + stage * 8);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -465,11 +619,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
         if (!ok) break;
-        tc_commit(acc_full);
+        tc_commit<CG>(smem_u32(acc_full));
         acc_ph ^= 1;
       }
       // drain: the commit arrives once every tcgen05 op this thread issued has completed
-      tc_commit(drain);
+      tc_commit_local<CG>(smem_u32(drain));
       const uint32_t a = smem_u32(drain);
       const unsigned long long t0 = globaltimer();
       while (!mbar_try(a, 0) && (long long)(globaltimer() - t0) < kWaitLimitNs) {
@@ -478,58 +632,38 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp < EPI_WARP0) {
     // ------------------------------------------------------------------------------------------ scale writers
     // Lane r of quadrant q writes TMEM lane 32q + r: for SFA the 16 bytes at r * 16 of each 512-byte chunk (rows
-    // r, r+32, r+64, r+96 x 4 scales), for SFB the same from the two 128-row groups (8 columns). Every quadrant
-    // holds the same values: the block-scaled MMA reads the copy of its own lane quadrant. The bytes come straight
-    // from global memory (L2-resident scale arrays), so the stage's smem holds only the operand tiles.
-    if (FP4) {
-      const uint32_t q = warp & 3;
-      const uint32_t tq = tmem + ((q * 32) << 16);
-      int stage = 0;
-      uint32_t ph = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-        const int mb = tile % p.num_m, nb = tile / p.num_m;
-        const int g0 = MODE == MODE_FP4_SWIGLU ? nb : 2 * nb;
-        const int g1 = MODE == MODE_FP4_SWIGLU ? (p.N >> 7) + nb : 2 * nb + 1;
-        const uint4* pa = reinterpret_cast<const uint4*>(p.sfa + (size_t)mb * p.sf_chunks * 512) + lane;
-        const uint4* pb0 = reinterpret_cast<const uint4*>(p.sfb + (size_t)g0 * p.sf_chunks * 512) + lane;
-        const uint4* pb1 = reinterpret_cast<const uint4*>(p.sfb + (size_t)g1 * p.sf_chunks * 512) + lane;
-        const bool has_g0 = g0 < p.sfb_groups, has_g1 = g1 < p.sfb_groups;
-        for (int ks = 0; ks < p.num_ks; ++ks) {
+    // r, r+32, r+64, r+96 x 4 scales), for SFB the same from the tile's two 128-row B groups (8 columns). Every
+    // quadrant holds the same values: the block-scaled MMA reads the copy of its own lane quadrant. With a CTA
+    // pair each CTA writes its own A rows' scales and all 256 B columns' scales into its own TMEM. Then the warp
+    // tells the group's MMA thread (on the leader) that this CTA's part of the stage is in place.
+    const uint32_t q = warp & 3;
+    const uint32_t tq = tmem + ((q * 32) << 16);
+    int stage = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int tile = grp; FP4 && ok && tile < p.num_tiles; tile += ngrp) {
+      for (int ks = 0; ks < p.num_ks; ++ks) {
+        // the stage's scales landed; its TMEM scale buffer is free too: the producer re-armed the stage only after
+        // the MMAs of its previous use completed
+        if (!mbar_wait<false>(CG == 2 ? sff + stage : full + stage, ph, p.err, 0x401)) {
+          ok = false;
+          break;
+        }
+        if (FP4) {
           const int kb_here = min(4, p.kb_total - ks * 4);
+          const uint4* a4 = reinterpret_cast<const uint4*>(sSFA + stage * SFA_BYTES) + lane;
+          const uint4* b4 = reinterpret_cast<const uint4*>(sSFB + stage * SFB_BYTES) + lane;
+          // all shared-memory reads first: the TMEM stores below are asm with a memory clobber, and a read placed
+          // after one of them would wait out its own latency before the next store
           uint4 va[4], vb0[4], vb1[4];
-          if (SF_GLOBAL) {
 #pragma unroll
-            for (int kb = 0; kb < 4; ++kb) {     // loads first: their latency overlaps the wait below
-              const int c = (ks * 4 + kb) * 32;
-              const bool in = kb < kb_here;
-              va[kb] = in ? __ldg(pa + c) : make_uint4(0, 0, 0, 0);
-              vb0[kb] = in && has_g0 ? __ldg(pb0 + c) : make_uint4(0, 0, 0, 0);
-              vb1[kb] = in && has_g1 ? __ldg(pb1 + c) : make_uint4(0, 0, 0, 0);
-            }
-            // the stage's TMEM scale buffer is free once the MMAs of its previous use completed
-            if (!mbar_wait<false>(empty + stage, ph ^ 1, p.err, 0x401)) {
-              ok = false;
-              break;
-            }
-          } else {
-            // the stage's scales landed in smem (and its TMEM buffer's previous MMAs are done: the producer
-            // re-armed the stage only after they completed)
-            if (!mbar_wait<false>(full + stage, ph, p.err, 0x401)) {
-              ok = false;
-              break;
-            }
-            const uint4* a4 = reinterpret_cast<const uint4*>(sSFA + stage * SFA_BYTES) + lane;
-            const uint4* b4 = reinterpret_cast<const uint4*>(sSFB + stage * SFB_BYTES) + lane;
-#pragma unroll
-            for (int kb = 0; kb < 4; ++kb) {
-              va[kb] = a4[kb * 32];
-              vb0[kb] = b4[kb * 32];
-              vb1[kb] = b4[128 + kb * 32];
-            }
+          for (int kb = 0; kb < 4; ++kb) {
+            va[kb] = a4[kb * 32];
+            vb0[kb] = b4[kb * 32];
+            vb1[kb] = b4[128 + kb * 32];
           }
-          tc_fence_after();
           const uint32_t col = SF_COL + stage * SF_STAGE_COLS;
+          tc_fence_after();
 #pragma unroll
           for (int kb = 0; kb < 4; ++kb) {
             if (kb < kb_here) {
@@ -539,12 +673,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
           tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(sf_full + stage);
-          if (++stage == STAGES) {
-            stage = 0;
-            ph ^= 1;
-          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          if (CG == 2 && rank != 0) mbar_arrive_cluster(ready_l + stage * 8);   // the leader's barrier
+          else mbar_arrive(ready + stage);
+        }
+        if (++stage == STAGES) {
+          stage = 0;
+          ph ^= 1;
         }
       }
     }
@@ -552,15 +689,16 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int half = (warp - EPI_WARP0) >> 2;      // which half of the tile's columns this warp drains
-    const int r = q * 32 + lane;                   // row inside the tile == TMEM lane
+    const int r = q * 32 + lane;                   // row inside this CTA's 128 rows == TMEM lane
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
     uint8_t* stg = sOut + (warp - EPI_WARP0) * OUT_WARP_BYTES;   // this warp's 32 x 128-byte staging box
     uint32_t acc_ph = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+    for (int tile = grp; tile < p.num_tiles; tile += ngrp) {
       if (!mbar_wait<false>(acc_full, acc_ph, p.err, 0x301)) break;
       tc_fence_after();
       const int mb = tile % p.num_m, nb = tile / p.num_m;
-      const int64_t m = (int64_t)mb * BM + r;
+      const int row0 = mb * (BM * CG) + (int)rank * BM;            // this CTA's first output row
+      const int64_t m = (int64_t)row0 + r;
       if (MODE == MODE_FP4_SWIGLU) {
         // this warp: hidden columns [half*64, half*64 + 64) of the tile = gate and up accumulator columns
         const int F = p.N;
@@ -590,7 +728,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(acc_empty);                    // accumulator drained: the next tile's MMAs may start
+        __syncwarp();
+        if (lane == 0) {                           // drained: the next tile's MMAs may start
+          if (CG == 2 && rank != 0) mbar_arrive_cluster(acc_empty_l);
+          else mbar_arrive(acc_empty);
+        }
         if (lane == 0) tma_store_wait_read();      // the staging box is free once the previous store read it
         __syncwarp();
         if (m < p.M) {
@@ -622,15 +764,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           dc[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
           dc[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
           *reinterpret_cast<uint32_t*>(p.h_sf + sf_tiled_offset(m, col0 / 16, F / 64)) = sfw;
-        } else {
+        } else if (m < (int64_t)p.sfa_groups * 128) {
           *reinterpret_cast<uint32_t*>(p.h_sf + sf_tiled_offset(m, col0 / 16, F / 64)) = 0u;
         }
         // 32 rows x 32 bytes of codes for this warp (rows past M are clipped by the tensor map)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
-        if (lane == 0 && mb * BM + q * 32 < p.M) tma_store_2d(&tmY, stg, (int)(col0 / 2), mb * BM + q * 32);
+        if (lane == 0 && row0 + q * 32 < p.M) tma_store_2d(&tmY, stg, (int)(col0 / 2), row0 + q * 32);
       } else {
-        // this warp: output columns [half*128, half*128 + 128) of the tile, drained 64 at a time
+        // this warp: output columns [half*128, half*128 + 128) of the tile, drained 32 at a time
         float scale = p.alpha;
         if (MODE == MODE_FP8) scale = __ldg(p.a_scale) * (p.b_per_channel ? 1.0f : __ldg(p.b_scale));
         const int n_base = nb * BN + half * 128;
@@ -655,7 +797,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(acc_empty);                    // accumulator drained: the next tile's MMAs may start
+        __syncwarp();
+        if (lane == 0) {                           // drained: the next tile's MMAs may start
+          if (CG == 2 && rank != 0) mbar_arrive_cluster(acc_empty_l);
+          else mbar_arrive(acc_empty);
+        }
         // two 64-column boxes through the 128-byte-swizzled staging buffer and TMA stores (coalesced, async,
         // clipped at the M / N edges); the buffer is reused once the previous store has read it
 #pragma unroll
@@ -669,8 +815,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                            pk[c * 32 + 4 * ch + 3]);
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
-          if (lane == 0 && n_base + c * 64 < p.N && mb * BM + q * 32 < p.M)
-            tma_store_2d(&tmY, stg, n_base + c * 64, mb * BM + q * 32);
+          if (lane == 0 && n_base + c * 64 < p.N && row0 + q * 32 < p.M)
+            tma_store_2d(&tmY, stg, n_base + c * 64, row0 + q * 32);
         }
       }
       acc_ph ^= 1;
@@ -679,29 +825,58 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if (CG == 2) {
+    // neither CTA releases TMEM or exits while the other may still signal it
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    if (CG == 2)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
 }
 
-template <int MODE>
+template <int MODE, int CG>
 tfb_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty, const Params& p,
                   cudaStream_t s) {
   const DeviceInfo* di;
   tfb_status st = device_info(&di);
   if (st != TFB_OK) return st;
-  static bool attr_set[64];
-  if (!attr_set[di->device]) {
-    TFB_CUDA(cudaFuncSetAttribute(gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(MODE)));
-    attr_set[di->device] = true;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = Cfg<MODE, CG>::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = CG == 2 ? 1 : 0;
+  // Persistent grid: as many groups as can be resident at once. A CTA pair must sit inside one GPC, so on parts
+  // whose GPCs hold an odd number of usable SMs fewer than sm_count / 2 pairs fit; a larger grid would run its
+  // extra pairs as a second wave after the first ones finished all their tiles.
+  static int resident[64];
+  if (!resident[di->device]) {
+    TFB_CUDA(cudaFuncSetAttribute(gemm_kernel<MODE, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  Cfg<MODE, CG>::SMEM));
+    int n = di->sm_count;
+    if (CG == 2) {
+      cfg.gridDim = dim3(di->sm_count);
+      TFB_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_kernel<MODE, CG>, &cfg));
+      if (n <= 0) return fail(TFB_CUDA_ERR, "gemm: no CTA pair of this kernel fits on the device");
+    }
+    resident[di->device] = min(n, di->sm_count / CG);
   }
-  const int grid = p.num_tiles < di->sm_count ? p.num_tiles : di->sm_count;
-  if (grid == 0) return TFB_OK;
-  gemm_kernel<MODE><<<grid, THREADS, smem_bytes(MODE), s>>>(ta, tb, ty, p);
-  TFB_CUDA(cudaGetLastError());
+  const int groups = min(p.num_tiles, resident[di->device]);
+  if (groups == 0) return TFB_OK;
+  cfg.gridDim = dim3(groups * CG);
+  TFB_CUDA(cudaLaunchKernelEx(&cfg, gemm_kernel<MODE, CG>, ta, tb, ty, p));
   return TFB_OK;
 }
 
@@ -714,10 +889,29 @@ tfb_status check_common(int64_t M, int64_t N, int64_t K, const char* who) {
   return TFB_OK;
 }
 
-void fill_tiles(Params& p, int64_t M, int64_t ncols_per_tile, int64_t N) {
-  p.num_m = (int)((M + BM - 1) / BM);
+// CTAs per MMA group: pairs (cta_group::2, 256-row tiles) unless M fits one 128-row tile or TFB_CTA_GROUP=1.
+int cta_group(int64_t M) {
+  static int forced = -1;
+  if (forced < 0) {
+    const char* e = getenv("TFB_CTA_GROUP");
+    forced = e ? atoi(e) : 0;
+  }
+  return (forced == 1 || M <= BM) ? 1 : 2;
+}
+
+void fill_tiles(Params& p, int cg, int64_t M, int64_t ncols_per_tile, int64_t N) {
+  p.num_m = (int)((M + BM * cg - 1) / (BM * cg));
   p.num_n = (int)((N + ncols_per_tile - 1) / ncols_per_tile);
   p.num_tiles = p.num_m * p.num_n;
+  p.sfa_groups = (int)((M + BM - 1) / BM);
+}
+
+template <int MODE>
+tfb_status dispatch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ty, Params& p, int64_t M,
+                    int64_t ncols_per_tile, int64_t N, cudaStream_t s) {
+  const int cg = cta_group(M);
+  fill_tiles(p, cg, M, ncols_per_tile, N);
+  return cg == 2 ? launch<MODE, 2>(ta, tb, ty, p, s) : launch<MODE, 1>(ta, tb, ty, p, s);
 }
 
 }  // namespace
@@ -739,7 +933,6 @@ tfb_status gemm_nvfp4(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, c
   Params p{};
   p.M = (int)M;
   p.N = (int)N;
-  fill_tiles(p, M, BN, N);
   p.num_ks = (int)(K / 256 + (K % 256 ? 1 : 0));
   p.kb_total = (int)(K / 64);
   p.b_rows = (int)N;
@@ -751,7 +944,7 @@ tfb_status gemm_nvfp4(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, c
   p.ldy = ldy;
   p.alpha = alpha;
   p.err = di->err_word;
-  return launch<MODE_FP4>(ta, tb, ty, p, s);
+  return dispatch<MODE_FP4>(ta, tb, ty, p, M, BN, N, s);
 }
 
 tfb_status gemm_nvfp4_swiglu(const uint8_t* a, const uint8_t* a_sf, const uint8_t* gu, const uint8_t* gu_sf, int64_t M,
@@ -773,7 +966,6 @@ tfb_status gemm_nvfp4_swiglu(const uint8_t* a, const uint8_t* a_sf, const uint8_
   Params p{};
   p.M = (int)M;
   p.N = (int)F;
-  fill_tiles(p, M, 128, F);
   p.num_ks = (int)(K / 256 + (K % 256 ? 1 : 0));
   p.kb_total = (int)(K / 64);
   p.b_rows = (int)(2 * F);
@@ -790,7 +982,7 @@ tfb_status gemm_nvfp4_swiglu(const uint8_t* a, const uint8_t* a_sf, const uint8_
   p.err = di->err_word;
   CUtensorMap th;                                      // h codes: 32-byte x 32-row boxes, one per epilogue warp
   if ((st = make_tmap_2d(&th, h_codes, 1, F / 2, M, F / 2, 32, 32, false)) != TFB_OK) return st;
-  return launch<MODE_FP4_SWIGLU>(ta, tb, th, p, s);
+  return dispatch<MODE_FP4_SWIGLU>(ta, tb, th, p, M, 128, F, s);
 }
 
 tfb_status gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, int64_t K, const float* a_scale,
@@ -810,7 +1002,6 @@ tfb_status gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, in
   Params p{};
   p.M = (int)M;
   p.N = (int)N;
-  fill_tiles(p, M, BN, N);
   p.num_ks = (int)(K / 128);
   p.kb_total = (int)(K / 32);
   p.b_rows = (int)N;
@@ -820,7 +1011,7 @@ tfb_status gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, in
   p.b_scale = b_scale;
   p.b_per_channel = per_channel;
   p.err = di->err_word;
-  return launch<MODE_FP8>(ta, tb, ty, p, s);
+  return dispatch<MODE_FP8>(ta, tb, ty, p, M, BN, N, s);
 }
 
 }  // namespace tfb

@@ -150,3 +150,21 @@ def test_fp8_linear_api(dev):
         y = lin(x.to(dev))
         ref = ofp8.linear(x.float().numpy(), u8(lin.w8), lin.ws.cpu().numpy(), act)
         assert rel_l2(f32(y), ref) <= TOL_FP8
+
+
+def test_single_cta_kernels_for_large_m():
+    """For M > 128 the GEMMs run on CTA pairs; TFB_CTA_GROUP=1 (read once per process) selects the single-CTA
+    kernels instead. Re-run the shape, FP8 and SwiGLU-epilogue tests in a child process with it set."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    here = Path(__file__).resolve().parent
+    env = dict(os.environ, TFB_CTA_GROUP="1")
+    r = subprocess.run(
+        [sys.executable, "-m", "pytest", str(here / "test_gemm_gpu.py"), "-q", "-m", "gpu", "-p", "no:cacheprovider",
+         "-k", "gemm_nvfp4_shapes or gemm_fp8_config3 or swiglu_epilogue or fused_mlp"],
+        cwd=here.parent, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+    assert " passed" in r.stdout
