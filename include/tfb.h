@@ -103,6 +103,36 @@ tfb_status tfb_mlp_nvfp4(const void* x, int64_t M, int64_t K, int64_t F, float a
                          float g_down, float act_h, void* y, uint8_t* ws_xc, uint8_t* ws_xsf, uint8_t* ws_hc,
                          uint8_t* ws_hsf, void* stream);
 
+/* Size of the device array that tfb_mlp_nvfp4_static uses as scratch: 32 MiB, one array per device. */
+#define TFB_MLP_STATIC_SCRATCH_BYTES (32ll << 20)
+
+/* The fused MLP pair of tfb_mlp_nvfp4 without a workspace argument and without allocating device memory: the
+ * x codes/scales and hidden codes/scales live in a device array inside the library (TFB_MLP_STATIC_SCRATCH_BYTES
+ * per device). This entry point has no counterpart in the reference, whose fused MLP gets its intermediates from
+ * torch's allocator.
+ * It is meant for callers that cannot allocate: a host that reaches the library only through this C interface
+ * and holds nothing but the device pointers its engine handed over (no device allocator of its own); an engine
+ * whose device memory is a fixed budget managed by its own pool, where an allocation behind the pool's back could
+ * fail or upset its accounting; and latency-critical loops, where cudaMalloc / cudaFree can block the calling
+ * thread or wait for the device to go idle.
+ * Rules:
+ *  - Limit: the call needs round256(M*K/2) + round256(tfb_sf_tiled_bytes(M, K)) + round256(M*F/2) +
+ *    tfb_sf_tiled_bytes(M, F) bytes (round256 = up to a multiple of 256). More than TFB_MLP_STATIC_SCRATCH_BYTES
+ *    returns TFB_BAD_SHAPE with a message naming both figures; nothing is launched. Example: M = 4352, K = 3072,
+ *    F = 8192 needs 27.6 MB and fits; larger M must be split across calls or go through tfb_mlp_nvfp4.
+ *  - Set-up: the first call on a device looks up that device's copy of the array (cudaGetSymbolAddress, with the
+ *    device current) together with the library's other one-time per-device work (device query, kernel
+ *    attributes). Make the first call on each device before beginning any stream capture.
+ *  - One array per device: two calls that can be in flight at the same time on the same device (different
+ *    streams, or different host threads without ordering) race on it and corrupt each other's outputs. Issue
+ *    them on one stream or otherwise serialise them. Calls on one stream are ordered and safe.
+ *  - Nothing in the array has to start at zero and the library never clears it: every byte a call reads from it
+ *    was written earlier in the same call.
+ * Arguments, shape rules and results are those of tfb_mlp_nvfp4. */
+tfb_status tfb_mlp_nvfp4_static(const void* x, int64_t M, int64_t K, int64_t F, float act_x, const uint8_t* gu_codes,
+                                const uint8_t* gu_sf, float g_gu, const uint8_t* down_codes, const uint8_t* down_sf,
+                                float g_down, float act_h, void* y, void* stream);
+
 /* AdaLN modulate: per row of x [B*N, D] (batch b = row / N): y = LN(x) * (1 + scale[b]) (+ shift[b]), fp32
  * inside, eps inside the rsqrt; scale/shift are fp32 [B, D] (shift nullable). Outputs (each nullable, at least
  * one): out bf16 [B*N, D]; NVFP4 codes [B*N, D/2] + tiled scales of the bf16-rounded result under q_global.

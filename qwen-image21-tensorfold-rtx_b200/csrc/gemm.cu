@@ -27,6 +27,9 @@
 // No TMA multicast anywhere: each CTA loads its own operand tiles.
 #include <stdlib.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "tfb_common.cuh"
 
 namespace tfb {
@@ -1049,3 +1052,66 @@ tfb_status tfb_mlp_nvfp4(const void* x, int64_t M, int64_t K, int64_t F, float a
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------ fused MLP pair on static device scratch
+// tfb_mlp_nvfp4_static's scratch: one array per device (every context that loads the library gets its own copy),
+// carved per call into x codes | x scales | h codes | h scales at 256-byte boundaries.
+static __device__ __align__(256) uint8_t g_mlp_static_scratch[TFB_MLP_STATIC_SCRATCH_BYTES];
+
+namespace tfb {
+namespace {
+
+std::atomic<uint8_t*> g_mlp_scratch_addr[64];
+std::mutex g_mlp_scratch_mu;
+
+// The device address of the current device's copy of the array, looked up once per device (with that device
+// current, as cudaGetSymbolAddress requires) and cached.
+tfb_status mlp_static_scratch(uint8_t** out) {
+  const DeviceInfo* di;
+  tfb_status st = device_info(&di);
+  if (st != TFB_OK) return st;
+  uint8_t* p = g_mlp_scratch_addr[di->device].load(std::memory_order_acquire);
+  if (!p) {
+    std::lock_guard<std::mutex> lock(g_mlp_scratch_mu);
+    p = g_mlp_scratch_addr[di->device].load(std::memory_order_relaxed);
+    if (!p) {
+      void* a = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&a, g_mlp_static_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress (tfb_mlp_nvfp4_static scratch)");
+      if (!a || !aligned(a, 256)) return fail(TFB_CUDA_ERR, "tfb_mlp_nvfp4_static: scratch address unusable");
+      p = static_cast<uint8_t*>(a);
+      g_mlp_scratch_addr[di->device].store(p, std::memory_order_release);
+    }
+  }
+  *out = p;
+  return TFB_OK;
+}
+
+constexpr int64_t round256(int64_t n) { return (n + 255) / 256 * 256; }
+
+}  // namespace
+}  // namespace tfb
+
+extern "C" tfb_status tfb_mlp_nvfp4_static(const void* x, int64_t M, int64_t K, int64_t F, float act_x,
+                                           const uint8_t* gu_codes, const uint8_t* gu_sf, float g_gu,
+                                           const uint8_t* down_codes, const uint8_t* down_sf, float g_down,
+                                           float act_h, void* y, void* stream) {
+  constexpr int64_t kDimMax = (int64_t)1 << 30;
+  if (M < 0 || K <= 0 || F <= 0 || K % 64 || F % 64 || M > kDimMax || K > kDimMax || F > kDimMax)
+    return tfb::fail(TFB_BAD_SHAPE, "tfb_mlp_nvfp4_static: bad shape M=%lld K=%lld F=%lld", (long long)M,
+                     (long long)K, (long long)F);
+  const int64_t o_xsf = tfb::round256(M * (K / 2));
+  const int64_t o_hc = o_xsf + tfb::round256(tfb_sf_tiled_bytes(M, K));
+  const int64_t o_hsf = o_hc + tfb::round256(M * (F / 2));
+  const int64_t need = o_hsf + tfb_sf_tiled_bytes(M, F);
+  if (need > TFB_MLP_STATIC_SCRATCH_BYTES)
+    return tfb::fail(TFB_BAD_SHAPE,
+                     "tfb_mlp_nvfp4_static: M=%lld K=%lld F=%lld needs %lld bytes of scratch, more than the "
+                     "%lld-byte static array; split M across calls or use tfb_mlp_nvfp4 with a workspace",
+                     (long long)M, (long long)K, (long long)F, (long long)need, (long long)TFB_MLP_STATIC_SCRATCH_BYTES);
+  uint8_t* base = nullptr;
+  const tfb_status st = tfb::mlp_static_scratch(&base);
+  if (st != TFB_OK) return st;
+  return tfb_mlp_nvfp4(x, M, K, F, act_x, gu_codes, gu_sf, g_gu, down_codes, down_sf, g_down, act_h, y, base,
+                       base + o_xsf, base + o_hc, base + o_hsf, stream);
+}

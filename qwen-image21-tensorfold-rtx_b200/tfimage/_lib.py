@@ -35,6 +35,8 @@ SIGNATURES = {
                               c_vp],
     "tfb_mlp_nvfp4": [c_vp, c_i64, c_i64, c_i64, c_float, c_vp, c_vp, c_float, c_vp, c_vp, c_float, c_float, c_vp,
                       c_vp, c_vp, c_vp, c_vp, c_vp],
+    "tfb_mlp_nvfp4_static": [c_vp, c_i64, c_i64, c_i64, c_float, c_vp, c_vp, c_float, c_vp, c_vp, c_float, c_float,
+                             c_vp, c_vp],
     "tfb_adaln": [c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_float, c_vp, c_float, c_vp, c_vp, c_vp],
     "tfb_rms_rope": [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_float, c_vp, c_i64,
                      c_i64, c_vp],
@@ -43,6 +45,7 @@ SIGNATURES = {
 RESTYPES = {"tfb_version": c_int, "tfb_last_error": ctypes.c_char_p, "tfb_sf_tiled_bytes": c_i64}
 
 SF_ROWS, SF_TILED = 0, 1
+MLP_STATIC_SCRATCH_BYTES = 32 << 20   # TFB_MLP_STATIC_SCRATCH_BYTES
 STATUS = {0: "OK", 1: "BAD_SHAPE", 2: "BAD_ALIGN", 3: "BAD_ARCH", 4: "DEVICE_TIMEOUT", 5: "CUDA_ERR", 6: "BAD_ARG"}
 
 _lib = None
@@ -203,6 +206,21 @@ def mlp_workspace(M: int, K: int, F: int, device) -> tuple[torch.Tensor, ...]:
     u8 = dict(dtype=torch.uint8, device=device)
     return (torch.empty((M, K // 2), **u8), torch.empty((sf_tiled_bytes(M, K),), **u8),
             torch.empty((M, F // 2), **u8), torch.empty((sf_tiled_bytes(M, F),), **u8))
+
+
+def mlp_nvfp4_static(x, F: int, act_x: float, gu_codes, gu_sf, g_gu: float, down_codes, down_sf, g_down: float,
+                     act_h: float, out=None) -> torch.Tensor:
+    """mlp_nvfp4 on the library's per-device static scratch (tfb_mlp_nvfp4_static): no workspace is allocated.
+    Calls that may overlap on one device (different streams) must be serialised by the caller."""
+    _cuda(x, gu_codes, gu_sf, down_codes, down_sf)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or not x.is_contiguous():
+        raise TfbError("mlp_nvfp4_static takes a contiguous 2-D bf16 tensor")
+    M, K = x.shape
+    y = torch.empty((M, K), dtype=torch.bfloat16, device=x.device) if out is None else out
+    check(load().tfb_mlp_nvfp4_static(x.data_ptr(), M, K, F, float(act_x), gu_codes.data_ptr(), gu_sf.data_ptr(),
+                                      float(g_gu), down_codes.data_ptr(), down_sf.data_ptr(), float(g_down),
+                                      float(act_h), y.data_ptr(), _stream(x)))
+    return y
 
 
 def adaln(x, scale, shift, eps: float, out=None, q_global: float | None = None, codes=None, sf=None):
