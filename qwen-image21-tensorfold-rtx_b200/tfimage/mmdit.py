@@ -1,0 +1,268 @@
+"""Synthetic double-stream MMDiT on the tfimage API: the DiT step that the quantized-linear path runs inside.
+
+Shape and dataflow follow the reference DiT (tfimage/qwen_image21.py) at the sizes of the synthetic benchmark model:
+28 blocks, hidden 3072, 24 heads x 128, SwiGLU 8192, separate image and text QKV / O / MLP weights, all weights
+N(0, 0.02) from a seed (no checkpoint), RMS-norm weights N(1, 0.05). A latent [16, 128, 128] patchified 2 x 2 is
+the model input [B, 64, 64, 64] (4096 tokens); the prompt is a [256, 3584] context.
+
+* Prefix (qwen_image21.py:218-255): the text rows run through the text-stream weights once per prompt, modulated at
+  t = 0 and attending causally among themselves; every block's keys and values are kept.
+* Step (qwen_image21.py:259-299, _block :204-216): only the image rows run. Per block: AdaLN (+ shift) fused with
+  the NVFP4 quantizer of the qkv input, qkv GEMM, RMSNorm + RoPE of q and k (k written behind the kept prefix in
+  one key buffer, v copied beside it), SDPA over [prefix, image], out GEMM, gated residual, AdaLN fused with the
+  quantizer of the MLP input, the fused gate/up SwiGLU -> NVFP4 -> down pair, gated residual.
+* Sampler: flow-matching Euler on shifted sigmas (sampling.py:12-31).
+
+Linears are ``linear.make(kind, w)`` modules; static input scales come from ``calibrate`` (the reference's
+calibrate.py procedure: a dynamic-scale run, then 4 x the largest input scale seen per layer).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch.nn.attention import SDPBackend, sdpa_kernel
+
+from . import kernels as K
+from . import linear as L
+
+
+@dataclass(frozen=True)
+class DitConfig:
+    layers: int = 28
+    dim: int = 3072
+    heads: int = 24
+    head_dim: int = 128
+    mlp: int = 8192
+    in_ch: int = 64            # 16 latent channels x 2 x 2 patch
+    txt_dim: int = 3584
+    axes: tuple[int, int, int] = (16, 56, 56)
+    theta: float = 10000.0
+    eps: float = 1e-6
+
+
+SHIFT = 0.69                   # sampling.py:7
+
+
+def sigmas(steps: int, shift: float = SHIFT, table: int = 10000) -> list[float]:
+    """Shifted flow-matching sigmas of the "simple" schedule plus a final 0 (sampling.py:12-16)."""
+    t = torch.arange(1, table + 1, dtype=torch.float32) / table
+    s = math.exp(shift) / (math.exp(shift) + (1 / t - 1))
+    stride = table / steps
+    return [float(s[-(1 + int(i * stride))]) for i in range(steps)] + [0.0]
+
+
+def rope_table(ids: torch.Tensor, cfg: DitConfig) -> tuple[torch.Tensor, torch.Tensor]:
+    """ids [N, 3] -> cos, sin fp32 [N, head_dim / 2]; per axis the frequencies theta^-(2i/d) in fp64
+    (qwen_image21.py:63-72)."""
+    parts = []
+    for axis, d in enumerate(cfg.axes):
+        expo = torch.linspace(0, (d - 2) / d, steps=d // 2, dtype=torch.float64, device=ids.device)
+        parts.append(ids[:, axis].to(torch.float64)[:, None] * (1.0 / cfg.theta ** expo)[None])
+    a = torch.cat(parts, dim=1)
+    return torch.cos(a).float(), torch.sin(a).float()
+
+
+def image_ids(h: int, w: int, pos: int, device) -> torch.Tensor:
+    """[h*w, 3] ids of a target latent grid: (pos, row, col) centred on the grid (qwen_image21.py:164-169)."""
+    hh = torch.arange(h, device=device, dtype=torch.float32) - (h - h // 2)
+    ww = torch.arange(w, device=device, dtype=torch.float32) - (w - w // 2)
+    return torch.stack([torch.full((h, w), float(pos), device=device), hh[:, None].expand(h, w),
+                        ww[None, :].expand(h, w)], dim=-1).reshape(-1, 3)
+
+
+def text_ids(n: int, device) -> torch.Tensor:
+    """Sequential positions on all three axes (qwen_image21.py:232)."""
+    return torch.arange(n, device=device, dtype=torch.float32)[:, None].expand(n, 3)
+
+
+@dataclass
+class Block:
+    qkv: L.Linear
+    out: L.Linear
+    gate_up: L.Linear
+    down: L.Linear
+    norm_q: torch.Tensor       # fp32 [head_dim]
+    norm_k: torch.Tensor
+
+
+@dataclass
+class Prefix:
+    kv: list                   # per block (k, v) [1, P, H, D] bf16
+    length: int
+    next_pos: int
+
+
+def _sdpa(q, k, v, causal=False):
+    with sdpa_kernel([SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION],
+                     set_priority=True):
+        return F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+
+
+class SynthMMDiT:
+    """The synthetic MMDiT with NVFP4 (or ``kind``) linears; weights generated on ``device`` from ``seed``."""
+
+    def __init__(self, cfg: DitConfig = DitConfig(), kind: str = "nvfp4", device="cuda", seed: int = 0):
+        self.cfg, self.kind, self.device = cfg, kind, torch.device(device)
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        D = cfg.dim
+
+        def rnd(*shape, std=0.02, mean=0.0):
+            t = torch.randn(shape, generator=g, device=self.device, dtype=torch.float32)
+            return (t * std + mean).to(torch.bfloat16)
+
+        self.t1, self.t2 = rnd(D, 256), rnd(D, D)                # timestep embedder
+        self.mod_img, self.mod_txt = rnd(6 * D, D), rnd(6 * D, D)
+        self.img_in, self.proj_out, self.norm_out = rnd(D, cfg.in_ch), rnd(cfg.in_ch, D), rnd(D, D)
+        self.txt_norm = (torch.randn((cfg.txt_dim,), generator=g, device=self.device) * 0.05 + 1.0).float()
+        self.txt_in1, self.txt_in2 = rnd(D, cfg.txt_dim), rnd(D, D)
+        self.img_blocks: list[Block] = []
+        self.txt_blocks: list[Block] = []
+        H = cfg.heads * cfg.head_dim
+        for _ in range(cfg.layers):
+            for blocks in (self.img_blocks, self.txt_blocks):
+                lin = lambda *s: L.make(kind, rnd(*s))           # noqa: E731  (bf16 copy freed at once)
+                blocks.append(Block(lin(3 * H, D), lin(D, H), lin(2 * cfg.mlp, D), lin(D, cfg.mlp),
+                                    (torch.randn((cfg.head_dim,), generator=g, device=self.device) * 0.05 + 1).float(),
+                                    (torch.randn((cfg.head_dim,), generator=g, device=self.device) * 0.05 + 1).float()))
+
+    # ------------------------------------------------------------------------------------------- pieces
+    def linears(self):
+        for stream, blocks in (("img", self.img_blocks), ("txt", self.txt_blocks)):
+            for i, b in enumerate(blocks):
+                for name in ("qkv", "out", "gate_up", "down"):
+                    yield f"{stream}.{i}.{name}", getattr(b, name)
+
+    def nbytes(self) -> int:
+        return sum(lin.nbytes() for _, lin in self.linears())
+
+    def _temb(self, t: torch.Tensor) -> torch.Tensor:
+        """t [B] in [0, 1] -> timestep embedding [B, dim] (sinusoidal 256 -> linear -> silu -> linear)."""
+        half = 128
+        freqs = torch.exp(-math.log(10000.0) * torch.arange(half, dtype=torch.float32, device=t.device) / half)
+        args = (t.float() * 1000.0)[:, None] * freqs[None]
+        emb = torch.cat([torch.cos(args), torch.sin(args)], dim=-1).to(torch.bfloat16)
+        return F.linear(F.silu(F.linear(emb, self.t1)), self.t2)
+
+    @staticmethod
+    def _mod(temb: torch.Tensor, w: torch.Tensor):
+        """-> (shift1, scale1, gate1, shift2, scale2, gate2), each [B, 1, dim]; gates tanh'ed (qwen_image21.py:272)."""
+        m = F.linear(F.silu(temb), w).unsqueeze(1).chunk(6, dim=-1)
+        return m[0], m[1], m[2].tanh(), m[3], m[4], m[5].tanh()
+
+    def _block(self, b: Block, x, mod, cos, sin, kbuf, vbuf, causal=False, record: dict | None = None):
+        """One block on rows x [B, N, dim] (in place); k / v are written to kbuf / vbuf [B, P + N, H, D] rows P:.
+        ``record`` (tests): receives the intermediates; the fused AdaLN + quantize calls then also write their
+        bf16 result (the quantizer's input)."""
+        sh1, sc1, g1, sh2, sc2, g2 = mod
+        cfg = self.cfg
+        B, N, _ = x.shape
+        H, Dh, eps = cfg.heads, cfg.head_dim, cfg.eps
+        P = kbuf.shape[1] - N
+        rec = record is not None
+        bf = (lambda: torch.empty_like(x)) if rec else (lambda: None)   # noqa: E731
+        static = isinstance(b.qkv, L.Nvfp4Linear) and not b.qkv.dynamic
+        a_in = K.adaln(x, sc1, eps, shift=sh1, quant=b.qkv if static else None, out=bf() if static else None)
+        if not static:
+            a_in = a_in.reshape(B * N, -1)
+        qkv = b.qkv(a_in).view(B, N, 3, H, Dh)
+        q = torch.empty((B, N, H, Dh), dtype=torch.bfloat16, device=x.device)
+        K.rms_rope(qkv, 0, b.norm_q, cos, sin, eps, q)
+        K.rms_rope(qkv, 1, b.norm_k, cos, sin, eps, kbuf[:, P:])
+        vbuf[:, P:].copy_(qkv[:, :, 2])
+        o = _sdpa(q.transpose(1, 2), kbuf.transpose(1, 2), vbuf.transpose(1, 2), causal)
+        o = o.transpose(1, 2)
+        a = b.out(o.reshape(B * N, H * Dh)).view(B, N, -1)
+        if rec:
+            record.update(a_in=a_in, qkv=qkv, q=q, o=o, att=a, x_in=x.clone())
+        x.addcmul_(a, g1)
+        static = isinstance(b.gate_up, L.Nvfp4Linear) and not b.gate_up.dynamic
+        m_in = K.adaln(x, sc2, eps, shift=sh2, quant=b.gate_up if static else None, out=bf() if static else None)
+        y = L.swiglu_mlp(b.gate_up, b.down, m_in) if static else None
+        if y is None:
+            h = m_in.reshape(B * N, -1) if not isinstance(m_in, L.Nvfp4Act) else m_in
+            y = b.down(K.swiglu(b.gate_up(h)))
+        if rec:
+            record.update(x1=x.clone(), m_in=m_in, mlp=y.view(B, N, -1))
+        x.addcmul_(y.view(B, N, -1), g2)
+        return x
+
+    # ------------------------------------------------------------------------------------------- prefix
+    @torch.inference_mode()
+    def build_prefix(self, context: torch.Tensor) -> Prefix:
+        """context [1, L, txt_dim] -> the kept per-block text keys / values (t = 0 modulation, causal)."""
+        cfg = self.cfg
+        c = context.to(self.device).float()
+        c = c * torch.rsqrt(c.pow(2).mean(-1, keepdim=True) + cfg.eps) * self.txt_norm
+        x = F.linear(F.gelu(F.linear(c.to(torch.bfloat16), self.txt_in1), approximate="tanh"), self.txt_in2)
+        x = x.contiguous()
+        B, P, _ = x.shape
+        cos, sin = rope_table(text_ids(P, self.device), cfg)
+        mod = self._mod(self._temb(torch.zeros((B,), device=self.device)), self.mod_txt)
+        kv = []
+        for b in self.txt_blocks:
+            k = torch.empty((B, P, cfg.heads, cfg.head_dim), dtype=torch.bfloat16, device=self.device)
+            v = torch.empty_like(k)
+            x = self._block(b, x, mod, cos, sin, k, v, causal=True)
+            kv.append((k, v))
+        return Prefix(kv, P, P)
+
+    # ------------------------------------------------------------------------------------------- step
+    @torch.inference_mode()
+    def forward(self, x: torch.Tensor, t: torch.Tensor, prefix: Prefix, work: dict | None = None) -> torch.Tensor:
+        """x [B, 64, H, W] bf16, t [B] -> velocity [B, 64, H, W] bf16. ``work`` caches the step's buffers."""
+        cfg = self.cfg
+        B, C, Hh, Ww = x.shape
+        N, P = Hh * Ww, prefix.length
+        work = {} if work is None else work
+        key = (B, Hh, Ww, P)
+        if work.get("key") != key:
+            kbuf = torch.empty((B, P + N, cfg.heads, cfg.head_dim), dtype=torch.bfloat16, device=self.device)
+            work.update(key=key, kbuf=kbuf, vbuf=torch.empty_like(kbuf),
+                        rope=rope_table(image_ids(Hh, Ww, prefix.next_pos, self.device), cfg))
+        kbuf, vbuf = work["kbuf"], work["vbuf"]
+        cos, sin = work["rope"]
+        temb = self._temb(t)
+        mod = self._mod(temb, self.mod_img)
+        h = F.linear(x.flatten(2).transpose(1, 2), self.img_in).contiguous()
+        for b, (pk, pv) in zip(self.img_blocks, prefix.kv):
+            kbuf[:, :P].copy_(pk.expand(B, -1, -1, -1))
+            vbuf[:, :P].copy_(pv.expand(B, -1, -1, -1))
+            h = self._block(b, h, mod, cos, sin, kbuf, vbuf)
+        h = K.adaln(h, F.linear(F.silu(temb), self.norm_out).unsqueeze(1), cfg.eps)
+        out = F.linear(h, self.proj_out)
+        return out.transpose(1, 2).reshape(B, C, Hh, Ww)
+
+    __call__ = forward
+
+    @torch.inference_mode()
+    def sample(self, noise: torch.Tensor, prefix: Prefix, steps: int = 25, step_events=None) -> torch.Tensor:
+        """Flow-matching Euler from unit-Gaussian noise [B, 64, H, W] (sampling.py:19-31)."""
+        sig = sigmas(steps)
+        x = noise.float() * sig[0]
+        work: dict = {}
+        for i in range(steps):
+            t = torch.full((x.shape[0],), sig[i], device=x.device)
+            v = self.forward(x.to(torch.bfloat16), t, prefix, work).float()
+            x = x + (sig[i + 1] - sig[i]) * v
+            if step_events is not None:
+                step_events[i].record()
+        return x
+
+    # ------------------------------------------------------------------------------------------- calibration
+    @torch.inference_mode()
+    def calibrate(self, context: torch.Tensor, noise: torch.Tensor, steps: int = 4, margin: float = 4.0) -> dict:
+        """Static NVFP4 input scales (calibrate.py:19-33): run with dynamic scales, keep margin x the largest."""
+        lins = [(n, lin) for n, lin in self.linears() if isinstance(lin, L.Nvfp4Linear)]
+        for _, lin in lins:
+            lin.set_act(None)
+            lin.amax = 0.0
+        prefix = self.build_prefix(context)
+        self.sample(noise, prefix, steps)
+        acts = {n: lin.amax * margin for n, lin in lins}
+        for n, lin in lins:
+            lin.set_act(acts[n])
+        return acts
