@@ -208,6 +208,69 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------- DiT leg
+DIT_SEEDS, DIT_STEPS = 32, 25
+DIT_WORKLOAD = ("configs[4] synthetic double-stream MMDiT, NVFP4: 28 blocks, hidden 3072, 24 x 128 heads, SwiGLU "
+                "8192, separate image/text weights N(0, 0.02); latent [16, 128, 128] -> 4096 tokens; text [256, 3584] "
+                "N(0, 1), K/V prefix-cached once per prompt; 25 Euler steps; 32 seeds split across ranks")
+
+
+def dit_leg(world: int, rank: int, dev, barrier, reduce_max) -> dict:
+    """single-image DiT step latency at 4096 tokens, and images/s of the 25-step sampler over 32 seeds
+    split across the ranks (each rank a full weight replica, no collective on the data path)."""
+    import torch
+
+    from tfimage import mmdit
+
+    model = mmdit.SynthMMDiT(mmdit.DitConfig(), device=dev, seed=0)       # the same weights on every rank
+    g = torch.Generator().manual_seed(4)
+    ctx = torch.randn((1, 256, 3584), generator=g).to(dev)
+    model.calibrate(ctx, torch.randn((1, 64, 64, 64), generator=g).to(dev), steps=2)
+    counts = [DIT_SEEDS // world + (r < DIT_SEEDS % world) for r in range(world)]
+    first = sum(counts[:rank])
+    noise = torch.randn((DIT_SEEDS, 64, 64, 64), generator=torch.Generator().manual_seed(5))[first:first + counts[rank]]
+    noise = noise.to(dev)
+    stream = torch.cuda.current_stream(dev)
+    ev = lambda: torch.cuda.Event(enable_timing=True)                       # noqa: E731
+
+    # single-image step latency (B = 1, 4096 tokens attending to the 256-token prefix)
+    prefix = model.build_prefix(ctx)
+    x1 = noise[:1].to(torch.bfloat16)
+    t1 = torch.full((1,), 0.5, device=dev)
+    work: dict = {}
+    for _ in range(3):
+        model.forward(x1, t1, prefix, work)
+    barrier()
+    lat = [(ev(), ev()) for _ in range(10)]
+    for a, b in lat:
+        a.record(stream)
+        model.forward(x1, t1, prefix, work)
+        b.record(stream)
+    barrier()
+    step_ms = reduce_max(statistics.median(a.elapsed_time(b) for a, b in lat))
+
+    # throughput: this rank's seeds through the whole sampler, the prompt's prefix built inside the timed region
+    model.forward(noise.to(torch.bfloat16), torch.full((counts[rank],), 0.5, device=dev), prefix, {})
+    barrier()
+    a, b = ev(), ev()
+    with ClockSampler(dev.index) as clk:
+        a.record(stream)
+        prefix = model.build_prefix(ctx)
+        lat_out = model.sample(noise, prefix, DIT_STEPS)
+        b.record(stream)
+        barrier()
+    sample_s = reduce_max(a.elapsed_time(b)) / 1e3
+    ok = bool(torch.isfinite(lat_out).all())
+    return {"workload": DIT_WORKLOAD, "step_ms_at_4096_tokens": step_ms, "step_batch": 1,
+            "img_per_s": DIT_SEEDS / sample_s, "sample_s": sample_s, "seeds": DIT_SEEDS,
+            "seeds_per_rank": counts, "steps": DIT_STEPS, "scaling": "strong (32 seeds split across ranks)",
+            "parallelism": f"dp{world} (weight replica per rank, no collective)",
+            "weights_gb": model.nbytes() / 1e9, "launches_per_step": 9 * model.cfg.layers + 1,
+            "tensor_parallel_latency": None, "finite": ok, "clocks": clk.report(),
+            "timing": "CUDA events on the launching stream, max over ranks; latency = median of 10 steps after 3 "
+                      "warm-up; throughput = one timed 25-step sampler run (prefix included) after a warm-up step"}
+
+
 # ------------------------------------------------------------------------------------------------------ our arm
 def run_ours(args):
     import torch
@@ -297,6 +360,17 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e_value = world * FLOP_STEP / (float(e2e_t[0]) * 1e-3) / 1e12
+
+    def reduce_max(v: float) -> float:
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0])
+
+    dit = None
+    if not args.no_dit:
+        del flush
+        dit = dit_leg(world, rank, dev, barrier, reduce_max)
     status = _lib.device_status()
 
     if rank == 0:
@@ -333,6 +407,7 @@ def run_ours(args):
             "gpu_launches": 3 * args.steps,
             "clocks": clk.report(),
             "device_status": status,
+            "dit": dit,
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
@@ -349,6 +424,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-dit", action="store_true", help="skip the configs[4] DiT leg (latency + img/s)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
