@@ -86,6 +86,15 @@ tfb_status tfb_gemm_nvfp4(const uint8_t* a_codes, const uint8_t* a_sf, const uin
 tfb_status tfb_gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, int64_t K, const float* a_scale,
                         const float* b_scale, int b_per_channel, void* y, int64_t ldy, void* stream);
 
+/* NVFP4 GEMM fused with the block's gated residual: x[m, n] = bf16(fma(bf16(alpha * acc[m, n]),
+ * gate[m / rows_per_gate, n], x[m, n])) in place, i.e. x.addcmul_(linear(a), gate) of the reference block
+ * (tfimage/qwen_image21.py:213-215, torch computes addcmul as one fused multiply-add in fp32). x bf16 [M, N] with
+ * row stride ldx (elements, % 8 == 0); gate bf16 rows of N with stride ld_gate (% 8 == 0, 16-byte aligned), one row
+ * per rows_per_gate rows of x (the batch's tokens). Operand formats as tfb_gemm_nvfp4. */
+tfb_status tfb_gemm_nvfp4_resid(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* b_codes,
+                                const uint8_t* b_sf, int64_t M, int64_t N, int64_t K, float alpha, void* x,
+                                int64_t ldx, const void* gate, int64_t ld_gate, int64_t rows_per_gate, void* stream);
+
 /* Gate/up NVFP4 GEMM with a SwiGLU epilogue that writes NVFP4: W_gu = [gate; up] codes [2F, K].
  * h = bf16(bf16(silu(gate)) * up) with gate/up = bf16(alpha * acc), quantized under h_global into
  * h_codes [M, F/2] and h_sf (TFB_SF_TILED, rows = M, K = F). gu_out and h_out (both nullable) receive the

@@ -49,7 +49,9 @@ constexpr uint32_t ACC_COL = 0;               // accumulator: columns [0, 256)
 constexpr uint32_t SF_COL = 256;              // scales: one 48-column buffer per stage (SFA 4 x 4, SFB 4 x 8)
 constexpr uint32_t SF_STAGE_COLS = 48;
 
-enum Mode { MODE_FP4 = 0, MODE_FP8 = 1, MODE_FP4_SWIGLU = 2 };
+// MODE_FP4_RESID: NVFP4 GEMM whose epilogue adds the gated result into a bf16 residual stream in place,
+// y = bf16(fma(bf16(alpha * acc), gate[row / rows_per_gate, col], y)) -- torch's x.addcmul_(linear(a), gate).
+enum Mode { MODE_FP4 = 0, MODE_FP8 = 1, MODE_FP4_SWIGLU = 2, MODE_FP4_RESID = 3 };
 
 struct Params {
   int M, N;              // output rows / cols (swiglu: N = F, the hidden width)
@@ -73,6 +75,9 @@ struct Params {
   uint8_t* h_sf;         // tiled, K = F
   __nv_bfloat16* gu_out; // optional [M, 2F]
   __nv_bfloat16* h_out;  // optional [M, F]
+  const __nv_bfloat16* gate;   // resid: [rows / rows_per_gate, N] with row stride ld_gate
+  int64_t ld_gate;
+  int64_t rows_per_gate;
   int* err;
 };
 
@@ -411,7 +416,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* acc_full = sff + STAGES;
   uint64_t* acc_empty = acc_full + 1;       // leader: every epilogue warp of the group drained the accumulator
   uint64_t* drain = acc_empty + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* xbar = drain + 1;               // resid: per epilogue warp, its residual box landed in its staging
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint32_t rank = 0;                        // CTA rank inside the MMA group (0 = leader, issues the MMAs)
@@ -427,6 +433,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 8 * CG);
     mbar_init(drain, 1);
+    for (int w = 0; w < 8; ++w) mbar_init(xbar + w, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -696,12 +703,23 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
     uint8_t* stg = sOut + (warp - EPI_WARP0) * OUT_WARP_BYTES;   // this warp's 32 x 128-byte staging box
     uint32_t acc_ph = 0;
+    uint64_t* xb = xbar + (warp - EPI_WARP0);
+    uint32_t x_ph = 0, x_pending = 0;             // resid: parity of the next load; a load not yet waited for
     for (int tile = grp; tile < p.num_tiles; tile += ngrp) {
-      if (!mbar_wait<false>(acc_full, acc_ph, p.err, 0x301)) break;
-      tc_fence_after();
       const int mb = tile % p.num_m, nb = tile / p.num_m;
       const int row0 = mb * (BM * CG) + (int)rank * BM;            // this CTA's first output row
       const int64_t m = (int64_t)row0 + r;
+      const bool rows_live = row0 + q * 32 < p.M;
+      if (MODE == MODE_FP4_RESID && lane == 0 && rows_live && nb * BN + half * 128 < p.N) {
+        // the first residual box does not depend on the accumulator: fetch it while the tile's MMAs run (the
+        // staging box is free once the previous tile's last store has read it)
+        tma_store_wait_read();
+        mbar_expect_tx(xb, OUT_WARP_BYTES);
+        tma_load_2d(stg, &tmY, xb, nb * BN + half * 128, row0 + q * 32);
+        x_pending = 1;
+      }
+      if (!mbar_wait<false>(acc_full, acc_ph, p.err, 0x301)) break;
+      tc_fence_after();
       if (MODE == MODE_FP4_SWIGLU) {
         // this warp: hidden columns [half*64, half*64 + 64) of the tile = gate and up accumulator columns
         const int F = p.N;
@@ -809,20 +827,59 @@ __global__ void __launch_bounds__(THREADS, 1)
         // clipped at the M / N edges); the buffer is reused once the previous store has read it
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          if (lane == 0) tma_store_wait_read();
-          __syncwarp();
+          const bool live = n_base + c * 64 < p.N && rows_live;
+          if (MODE == MODE_FP4_RESID) {
+            if (!live) continue;
+            if (c == 1 && lane == 0) {               // second box: after the first one's store has read the box
+              tma_store_wait_read();
+              mbar_expect_tx(xb, OUT_WARP_BYTES);
+              tma_load_2d(stg, &tmY, xb, n_base + 64, row0 + q * 32);
+            }
+            __syncwarp();
+            // the load always lands (in-bounds tensor map); a wait that still runs out records its code
+            mbar_wait<false>(xb, x_ph, p.err, 0x302);
+            x_ph ^= 1;
+            x_pending = 0;
+            const int64_t grow = m < p.M ? m / p.rows_per_gate : 0;
+            const uint4* gp = reinterpret_cast<const uint4*>(p.gate + grow * p.ld_gate + n_base + c * 64);
 #pragma unroll
-          for (int ch = 0; ch < 8; ++ch)
-            *reinterpret_cast<uint4*>(stg + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
-                make_uint4(pk[c * 32 + 4 * ch], pk[c * 32 + 4 * ch + 1], pk[c * 32 + 4 * ch + 2],
-                           pk[c * 32 + 4 * ch + 3]);
+            for (int ch = 0; ch < 8; ++ch) {
+              uint4* px = reinterpret_cast<uint4*>(stg + lane * 128 + ((ch ^ (lane & 7)) << 4));
+              const uint4 xv = *px, gv = __ldg(gp + ch);
+              const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, gs[4] = {gv.x, gv.y, gv.z, gv.w};
+              uint32_t o[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t a2 = pk[c * 32 + 4 * ch + j];
+                const float lo = fmaf(__uint_as_float(a2 << 16), __uint_as_float(gs[j] << 16),
+                                      __uint_as_float(xs[j] << 16));
+                const float hi = fmaf(__uint_as_float(a2 & 0xFFFF0000u), __uint_as_float(gs[j] & 0xFFFF0000u),
+                                      __uint_as_float(xs[j] & 0xFFFF0000u));
+                o[j] = pack_bf16x2(lo, hi);
+              }
+              *px = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          } else {
+            if (lane == 0) tma_store_wait_read();
+            __syncwarp();
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch)
+              *reinterpret_cast<uint4*>(stg + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
+                  make_uint4(pk[c * 32 + 4 * ch], pk[c * 32 + 4 * ch + 1], pk[c * 32 + 4 * ch + 2],
+                             pk[c * 32 + 4 * ch + 3]);
+          }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
-          if (lane == 0 && n_base + c * 64 < p.N && row0 + q * 32 < p.M)
-            tma_store_2d(&tmY, stg, n_base + c * 64, row0 + q * 32);
+          if (lane == 0 && live) tma_store_2d(&tmY, stg, n_base + c * 64, row0 + q * 32);
         }
       }
       acc_ph ^= 1;
+    }
+    if (MODE == MODE_FP4_RESID && x_pending) {     // left the loop with a residual box still in flight
+      const uint32_t a = smem_u32(xb);
+      const unsigned long long t0 = globaltimer();
+      while (!mbar_try(a, x_ph) && (long long)(globaltimer() - t0) < kWaitLimitNs) {
+      }
     }
     if (lane == 0) tma_store_wait_all();
   }
@@ -950,6 +1007,43 @@ tfb_status gemm_nvfp4(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, c
   return dispatch<MODE_FP4>(ta, tb, ty, p, M, BN, N, s);
 }
 
+tfb_status gemm_nvfp4_resid(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf, int64_t M,
+                            int64_t N, int64_t K, float alpha, void* x, int64_t ldx, const void* gate,
+                            int64_t ld_gate, int64_t rows_per_gate, cudaStream_t s) {
+  tfb_status st = check_common(M, N, K, "gemm_nvfp4_resid");
+  if (st != TFB_OK) return st;
+  if (ldx < N || ldx % 8 || !aligned(x, 16) || !aligned(a_sf, 16) || !aligned(b_sf, 16))
+    return fail(TFB_BAD_ALIGN, "gemm_nvfp4_resid: x/ldx need 16-byte alignment, scales 16-byte aligned");
+  if (!gate || !aligned(gate, 16) || ld_gate < N || ld_gate % 8 || rows_per_gate < 1)
+    return fail(TFB_BAD_ARG, "gemm_nvfp4_resid: gate must be 16-byte aligned bf16 rows (ld_gate >= N, %% 8 == 0) "
+                "and rows_per_gate >= 1");
+  const DeviceInfo* di;
+  if ((st = device_info(&di)) != TFB_OK) return st;
+  if (M == 0) return TFB_OK;
+  CUtensorMap ta, tb, ty;
+  if ((st = make_tmap_u8(&ta, a, K / 2, M, K / 2, BKB, BM)) != TFB_OK) return st;
+  if ((st = make_tmap_u8(&tb, b, K / 2, N, K / 2, BKB, 128)) != TFB_OK) return st;
+  if ((st = make_tmap_2d(&ty, x, 2, N, M, ldx * 2, 64, 32, true)) != TFB_OK) return st;
+  Params p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.num_ks = (int)(K / 256 + (K % 256 ? 1 : 0));
+  p.kb_total = (int)(K / 64);
+  p.b_rows = (int)N;
+  p.sfa = a_sf;
+  p.sfb = b_sf;
+  p.sf_chunks = (int)(K / 64);
+  p.sfb_groups = (int)((N + 127) / 128);
+  p.y = x;
+  p.ldy = ldx;
+  p.alpha = alpha;
+  p.gate = static_cast<const __nv_bfloat16*>(gate);
+  p.ld_gate = ld_gate;
+  p.rows_per_gate = rows_per_gate;
+  p.err = di->err_word;
+  return dispatch<MODE_FP4_RESID>(ta, tb, ty, p, M, BN, N, s);
+}
+
 tfb_status gemm_nvfp4_swiglu(const uint8_t* a, const uint8_t* a_sf, const uint8_t* gu, const uint8_t* gu_sf, int64_t M,
                              int64_t F, int64_t K, float alpha, float h_g, uint8_t* h_codes, uint8_t* h_sf,
                              void* gu_out, void* h_out, cudaStream_t s) {
@@ -1024,6 +1118,13 @@ extern "C" {
 tfb_status tfb_gemm_nvfp4(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* b_codes, const uint8_t* b_sf,
                           int64_t M, int64_t N, int64_t K, float alpha, void* y, int64_t ldy, void* stream) {
   return tfb::gemm_nvfp4(a_codes, a_sf, b_codes, b_sf, M, N, K, alpha, y, ldy, static_cast<cudaStream_t>(stream));
+}
+
+tfb_status tfb_gemm_nvfp4_resid(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* b_codes,
+                                const uint8_t* b_sf, int64_t M, int64_t N, int64_t K, float alpha, void* x,
+                                int64_t ldx, const void* gate, int64_t ld_gate, int64_t rows_per_gate, void* stream) {
+  return tfb::gemm_nvfp4_resid(a_codes, a_sf, b_codes, b_sf, M, N, K, alpha, x, ldx, gate, ld_gate, rows_per_gate,
+                               static_cast<cudaStream_t>(stream));
 }
 
 tfb_status tfb_gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, int64_t K, const float* a_scale,

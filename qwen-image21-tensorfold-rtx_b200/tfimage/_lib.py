@@ -31,6 +31,8 @@ SIGNATURES = {
     "tfb_quant_fp8": [c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp],
     "tfb_gemm_nvfp4": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_vp, c_i64, c_vp],
     "tfb_gemm_fp8": [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_int, c_vp, c_i64, c_vp],
+    "tfb_gemm_nvfp4_resid": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_vp, c_i64, c_vp, c_i64, c_i64,
+                             c_vp],
     "tfb_gemm_nvfp4_swiglu": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_float, c_vp, c_vp, c_vp, c_vp,
                               c_vp],
     "tfb_mlp_nvfp4": [c_vp, c_i64, c_i64, c_i64, c_float, c_vp, c_vp, c_float, c_vp, c_vp, c_float, c_float, c_vp,
@@ -161,6 +163,19 @@ def gemm_nvfp4(a_codes, a_sf, b_codes, b_sf, M: int, N: int, K: int, alpha: floa
     check(load().tfb_gemm_nvfp4(a_codes.data_ptr(), a_sf.data_ptr(), b_codes.data_ptr(), b_sf.data_ptr(), M, N, K,
                                 float(alpha), y.data_ptr(), y.stride(0), _stream(a_codes)))
     return y
+
+
+def gemm_nvfp4_resid(a_codes, a_sf, b_codes, b_sf, M: int, N: int, K: int, alpha: float, x: torch.Tensor,
+                     gate: torch.Tensor, rows_per_gate: int) -> torch.Tensor:
+    """x[m, :] = bf16(fma(bf16(alpha * acc[m, :]), gate[m // rows_per_gate, :], x[m, :])) in place; x bf16 [M, N]
+    rows (unit column stride), gate bf16 [G, N] rows (unit column stride)."""
+    _cuda(a_codes, a_sf, b_codes, b_sf, x, gate)
+    if x.dtype != torch.bfloat16 or gate.dtype != torch.bfloat16 or x.stride(-1) != 1 or gate.stride(-1) != 1:
+        raise TfbError("gemm_nvfp4_resid: x and gate must be bf16 rows with unit column stride")
+    check(load().tfb_gemm_nvfp4_resid(a_codes.data_ptr(), a_sf.data_ptr(), b_codes.data_ptr(), b_sf.data_ptr(), M, N,
+                                      K, float(alpha), x.data_ptr(), x.stride(0), gate.data_ptr(), gate.stride(0),
+                                      int(rows_per_gate), _stream(x)))
+    return x
 
 
 def gemm_fp8(a8, b8, M: int, N: int, K: int, a_scale, b_scale, out=None) -> torch.Tensor:

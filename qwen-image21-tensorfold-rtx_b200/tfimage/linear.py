@@ -210,20 +210,53 @@ class Nvfp4Linear(Linear):
         codes, sf = _lib.quant_nvfp4(x, self.lin.act, _lib.SF_TILED)
         return Nvfp4Act(codes, sf, self.lin.act, x.shape[0], self.k)
 
-    def __call__(self, x) -> torch.Tensor:
+    def __call__(self, x, residual=None) -> torch.Tensor:
+        """y = x @ W^T (bf16). ``residual=(res, gate)`` (this build's addition): instead of returning y, update
+        ``res`` in place as ``res.addcmul_(y, gate)`` does (qwen_image21.py:213-215) inside the GEMM's epilogue,
+        and return ``res``."""
         q = x if isinstance(x, Nvfp4Act) else self.quantize(x)
         lin = self.lin
+        if residual is not None:
+            res, gate = residual
+            r2, g2, rows = _residual_views(res, gate, lin.n)
+            _lib.gemm_nvfp4_resid(q.codes, q.sf, lin.codes, lin.bs, q.m, lin.n, lin.k, q.act * lin.scale, r2, g2,
+                                  rows)
+            return res
         return _lib.gemm_nvfp4(q.codes, q.sf, lin.codes, lin.bs, q.m, lin.n, lin.k, q.act * lin.scale)
 
     def nbytes(self) -> int:
         return self.lin.words.numel() * 4 + self.lin.bs.numel()
 
 
-def swiglu_mlp(gate_up: Linear, down: Linear, x: torch.Tensor):
+def _residual_views(res: torch.Tensor, gate: torch.Tensor, n: int):
+    """res [..., n] bf16 (rows contiguous) and gate [B, 1, n] / [B, n] -> (res rows [M, n], gate rows [B, n], rows
+    per gate row); the residual stream is updated in place, so it must be a view the GEMM can write."""
+    if res.dtype != torch.bfloat16 or res.shape[-1] != n or res.stride(-1) != 1:
+        raise ValueError("residual stream must be bf16 [..., n] with unit column stride")
+    r2 = res.view(-1, n)
+    g2 = gate.reshape(-1, n)
+    if g2.dtype != torch.bfloat16:
+        g2 = g2.to(torch.bfloat16)
+    if g2.stride(-1) != 1:
+        g2 = g2.contiguous()
+    if r2.shape[0] % g2.shape[0]:
+        raise ValueError("residual rows must split evenly over the gate rows")
+    return r2, g2, r2.shape[0] // g2.shape[0]
+
+
+def gated_residual_(lin: Linear, x, res: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+    """res.addcmul_(lin(x), gate) -- fused into the GEMM epilogue for static NVFP4 layers, torch otherwise."""
+    if isinstance(lin, Nvfp4Linear):
+        return lin(x, residual=(res, gate))
+    return res.addcmul_(lin(x).view_as(res), gate)
+
+
+def swiglu_mlp(gate_up: Linear, down: Linear, x: torch.Tensor, residual=None):
     """linear.py:136-150: down(silu(gate) * up) in one pass when both are static-scale NVFP4: the gate/up GEMM's
     epilogue writes the SwiGLU rows as NVFP4 under down's input scale, so no bf16 [M, 2F] or [M, F] tensor exists.
     None if the layers cannot take it (the caller runs the unfused path). Needs F % 128 == 0 here (the reference:
-    F % 64)."""
+    F % 64). ``residual=(res, gate)`` (this build's addition): the down GEMM adds ``gate * y`` into ``res`` in place
+    (``res.addcmul_(y, gate)``) and ``res`` is returned."""
 
     if not (isinstance(gate_up, Nvfp4Linear) and isinstance(down, Nvfp4Linear)) or gate_up.dynamic or down.dynamic:
         return None
@@ -234,7 +267,8 @@ def swiglu_mlp(gate_up: Linear, down: Linear, x: torch.Tensor):
     gu = gate_up.lin
     h_codes, h_sf = _lib.gemm_nvfp4_swiglu(q.codes, q.sf, gu.codes, gu.bs, q.m, f, gu.k, q.act * gu.scale,
                                            down.lin.act)
-    return _lib.gemm_nvfp4(h_codes, h_sf, down.lin.codes, down.lin.bs, q.m, down.n, f, down.lin.act * down.lin.scale)
+    h = Nvfp4Act(h_codes, h_sf, down.lin.act, q.m, f)
+    return down(h, residual=residual)
 
 
 def make(kind: str, w: torch.Tensor, act: float | None = None) -> Linear:

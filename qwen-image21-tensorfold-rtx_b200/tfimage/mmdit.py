@@ -175,18 +175,24 @@ class SynthMMDiT:
         vbuf[:, P:].copy_(qkv[:, :, 2])
         o = _sdpa(q.transpose(1, 2), kbuf.transpose(1, 2), vbuf.transpose(1, 2), causal)
         o = o.transpose(1, 2)
-        a = b.out(o.reshape(B * N, H * Dh)).view(B, N, -1)
-        if rec:
+        if rec:                       # the branch output on its own, then torch's addcmul_ (tests)
+            a = b.out(o.reshape(B * N, H * Dh)).view(B, N, -1)
             record.update(a_in=a_in, qkv=qkv, q=q, o=o, att=a, x_in=x.clone())
-        x.addcmul_(a, g1)
+            x.addcmul_(a, g1)
+        else:                         # x += g1 * out(o), in the out GEMM's epilogue for NVFP4 layers
+            L.gated_residual_(b.out, o.reshape(B * N, H * Dh), x, g1)
         static = isinstance(b.gate_up, L.Nvfp4Linear) and not b.gate_up.dynamic
         m_in = K.adaln(x, sc2, eps, shift=sh2, quant=b.gate_up if static else None, out=bf() if static else None)
+        if rec:
+            x1 = x.clone()
+        if static and not rec and L.swiglu_mlp(b.gate_up, b.down, m_in, residual=(x, g2)) is not None:
+            return x                  # x += g2 * down(SwiGLU(gate_up(m))), in the down GEMM's epilogue
         y = L.swiglu_mlp(b.gate_up, b.down, m_in) if static else None
         if y is None:
             h = m_in.reshape(B * N, -1) if not isinstance(m_in, L.Nvfp4Act) else m_in
             y = b.down(K.swiglu(b.gate_up(h)))
         if rec:
-            record.update(x1=x.clone(), m_in=m_in, mlp=y.view(B, N, -1))
+            record.update(x1=x1, m_in=m_in, mlp=y.view(B, N, -1))
         x.addcmul_(y.view(B, N, -1), g2)
         return x
 

@@ -3,7 +3,7 @@
 import numpy as np
 import pytest
 import torch
-from _helpers import bf16_cpu, f32, quant_weight, rel_l2, u8
+from _helpers import bf16_cpu, f32, quant_weight, rel_l2, u8, ulp_bf16
 
 from oracle import fp8 as ofp8
 from oracle import fusions as ofu
@@ -168,3 +168,43 @@ def test_single_cta_kernels_for_large_m():
         cwd=here.parent, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
     assert " passed" in r.stdout
+
+
+@pytest.mark.parametrize("M,N,K,batches", [(300, 3072, 512, 3), (77, 256, 256, 1), (4096, 3072, 3072, 1)])
+def test_gemm_nvfp4_gated_residual_epilogue(dev, M, N, K, batches):
+    """tfb_gemm_nvfp4_resid: x += gate[b] * linear(a) inside the GEMM epilogue, against the unfused GEMM followed by
+    torch's addcmul_ (the reference block, qwen_image21.py:213-215) and against the oracle."""
+    x = bf16_cpu((M, K), seed=M + 5, outliers=4)
+    w = bf16_cpu((N, K), seed=N + 6, scale=0.02)
+    xc, xs = onv.quantize(x.float().numpy(), ga := onv.dynamic_act_global(float(x.float().abs().max())))
+    wc, ws, gw = quant_weight(w)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)   # noqa: E731
+    res = bf16_cpu((M, N), seed=M + 7, scale=4.0).to(dev)
+    rows = M // batches
+    gate = (bf16_cpu((batches, N), seed=M + 8, scale=0.3)).to(dev)
+    y = _lib.gemm_nvfp4(t(xc), t(onv.sf_tile(xs)), t(wc), t(onv.sf_tile(ws)), M, N, K, ga * gw)
+    ref = res.clone().view(batches, rows, N).addcmul_(y.view(batches, rows, N), gate.view(batches, 1, N)).view(M, N)
+    fused = res.clone()
+    _lib.gemm_nvfp4_resid(t(xc), t(onv.sf_tile(xs)), t(wc), t(onv.sf_tile(ws)), M, N, K, ga * gw, fused, gate, rows)
+    torch.cuda.synchronize()
+    a, b = f32(fused), f32(ref)
+    assert (a == b).mean() >= 0.9999
+    assert np.all(np.abs(a - b) <= ulp_bf16(b) + 1e-30)
+    y_or = onv.bf16_round(onv.gemm(xc, xs, ga, wc, ws, gw))
+    g_rows = np.repeat(f32(gate), rows, axis=0)
+    oracle = onv.bf16_round(f32(res) + y_or * g_rows)
+    assert rel_l2(a - f32(res), oracle - f32(res)) <= TOL_NVFP4
+
+
+def test_swiglu_mlp_gated_residual(dev):
+    M, K, F = 256, 512, 384
+    gu = L.Nvfp4Linear(bf16_cpu((2 * F, K), seed=61, scale=0.05).to(dev), act=0.004)
+    down = L.Nvfp4Linear(bf16_cpu((K, F), seed=62, scale=0.05).to(dev), act=0.001)
+    x = bf16_cpu((2, M // 2, K), seed=63).to(dev)
+    res = bf16_cpu((2, M // 2, K), seed=64, scale=3.0).to(dev)
+    gate = bf16_cpu((2, 1, K), seed=65, scale=0.5).to(dev)
+    y = L.swiglu_mlp(gu, down, x.view(M, K))
+    ref = res.clone().addcmul_(y.view(2, M // 2, K), gate)
+    out = res.clone()
+    assert L.swiglu_mlp(gu, down, x.view(M, K), residual=(out, gate)) is out
+    assert (f32(out) == f32(ref)).mean() >= 0.9999
