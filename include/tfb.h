@@ -157,6 +157,16 @@ tfb_status tfb_rms_rope(const void* src, int64_t B, int64_t N, int64_t H, int64_
                         int64_t src_off, const float* w, const float* cos, const float* sin, float eps, void* dst,
                         int64_t dst_sb, int64_t dst_sn, void* stream);
 
+/* The attention inputs of one block in one pass: src = qkv rows [B, N, 3, H, D] (element strides src_sb, src_sn;
+ * q, k, v at column offsets 0, H*D, 2*H*D) -> q = rms_rope(q part, wq), k = rms_rope(k part, wk), v = v part, each
+ * to its own strided destination (element strides *_sb, *_sn; dst + b*sb + n*sn + h*D + d). Same arithmetic as
+ * tfb_rms_rope per part. Replaces the reference block's two rms_rope calls plus the v copy into the kept-prefix
+ * buffer (tfimage/qwen_image21.py:180-191). D == 128. */
+tfb_status tfb_rms_rope_qkv(const void* src, int64_t B, int64_t N, int64_t H, int64_t D, int64_t src_sb,
+                            int64_t src_sn, const float* wq, const float* wk, const float* cos, const float* sin,
+                            float eps, void* q, int64_t q_sb, int64_t q_sn, void* k, int64_t k_sb, int64_t k_sn,
+                            void* v, int64_t v_sb, int64_t v_sn, void* stream);
+
 /* Standalone SwiGLU: gu bf16 [M, 2F] = [gate | up] -> out bf16 [M, F] = bf16(bf16(silu(gate)) * up).
  * Replaces the Triton _swiglu_kernel (tfimage/kernels.py:73-92). F % 8 == 0. */
 tfb_status tfb_swiglu(const void* gu, int64_t M, int64_t F, void* out, void* stream);

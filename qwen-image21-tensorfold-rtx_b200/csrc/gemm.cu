@@ -379,6 +379,22 @@ __device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bu
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 
+// Output tile -> (M block, N block). Tiles go in bands of kBandM M blocks; inside a band the M block changes fastest,
+// so the ~74-148 tiles in flight at once share a few B column blocks and all of the band's A rows. A band's A
+// (16 x 256 rows) stays in L2 while the band walks every N block and B is read once per band; with the plain
+// M-fastest order A was re-read from HBM once per N block when it did not fit in L2 (M = 131072: 13 GB per
+// gate/up launch).
+constexpr int kBandM = 16;
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  const int band_tiles = kBandM * num_n;
+  const int band = tile / band_tiles;
+  const int first = band * kBandM;
+  const int gm = min(kBandM, num_m - first);
+  const int idx = tile - band * band_tiles;
+  mb = first + idx % gm;
+  nb = idx / gm;
+}
+
 // --------------------------------------------------------------------------------------------------- the kernel
 // Pipeline depth per (mode, CTA group): an NVFP4 stage holds A 16 KB + B 16 KB per CTA of the group's B half
 // (1 CTA: the whole 32 KB B tile) + 6 KB of scales; FP8 stages have no scales. All fit beside the 32 KB epilogue
@@ -477,7 +493,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t last_ph = 0;    // bit s: parity of its last arming
       bool ok = true;
       for (int tile = grp; ok && tile < p.num_tiles; tile += ngrp) {
-        const int mb = tile % p.num_m, nb = tile / p.num_m;
+        int mb, nb;
+        tile_coords(tile, p.num_m, p.num_n, mb, nb);
         const int arow = mb * (BM * CG) + (int)rank * BM;             // this CTA's A rows
         int rb0, rb1;                                                  // the tile's two 128-row B groups
         if (MODE == MODE_FP4_SWIGLU) {
@@ -706,7 +723,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* xb = xbar + (warp - EPI_WARP0);
     uint32_t x_ph = 0, x_pending = 0;             // resid: parity of the next load; a load not yet waited for
     for (int tile = grp; tile < p.num_tiles; tile += ngrp) {
-      const int mb = tile % p.num_m, nb = tile / p.num_m;
+      int mb, nb;
+      tile_coords(tile, p.num_m, p.num_n, mb, nb);
       const int row0 = mb * (BM * CG) + (int)rank * BM;            // this CTA's first output row
       const int64_t m = (int64_t)row0 + r;
       const bool rows_live = row0 + q * 32 < p.M;

@@ -42,6 +42,8 @@ SIGNATURES = {
     "tfb_adaln": [c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_float, c_vp, c_float, c_vp, c_vp, c_vp],
     "tfb_rms_rope": [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_float, c_vp, c_i64,
                      c_i64, c_vp],
+    "tfb_rms_rope_qkv": [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_float, c_vp, c_i64,
+                         c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp],
     "tfb_swiglu": [c_vp, c_i64, c_i64, c_vp, c_vp],
 }
 RESTYPES = {"tfb_version": c_int, "tfb_last_error": ctypes.c_char_p, "tfb_sf_tiled_bytes": c_i64}
@@ -251,6 +253,15 @@ def rms_rope(src, part: int, w, cos, sin, eps: float, dst) -> None:
     check(load().tfb_rms_rope(src.data_ptr(), B, N, H, D, src.stride(0), src.stride(1), part * H * D, w.data_ptr(),
                               cos.data_ptr(), sin.data_ptr(), float(eps), dst.data_ptr(), dst.stride(0),
                               dst.stride(1), _stream(src)))
+
+
+def rms_rope_qkv(src, wq, wk, cos, sin, eps: float, q, k, v) -> None:
+    _cuda(src, wq, wk, cos, sin, q, k, v)
+    B, N, _, H, D = src.shape
+    check(load().tfb_rms_rope_qkv(src.data_ptr(), B, N, H, D, src.stride(0), src.stride(1), wq.data_ptr(),
+                                  wk.data_ptr(), cos.data_ptr(), sin.data_ptr(), float(eps), q.data_ptr(), q.stride(0),
+                                  q.stride(1), k.data_ptr(), k.stride(0), k.stride(1), v.data_ptr(), v.stride(0),
+                                  v.stride(1), _stream(src)))
 
 
 def swiglu(gu, out) -> None:

@@ -52,6 +52,21 @@ def rms_rope(src: torch.Tensor, part: int, w: torch.Tensor, cos: torch.Tensor, s
     _lib.rms_rope(src, part, w.float().contiguous(), cos.float().contiguous(), sin.float().contiguous(), eps, dst)
 
 
+def rms_rope_qkv(src: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                 eps: float, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+    """This build's addition: ``rms_rope(src, 0, wq, ...) -> q``, ``rms_rope(src, 1, wk, ...) -> k`` and
+    ``v.copy_(src[:, :, 2])`` in one pass (the reference block's attention inputs, qwen_image21.py:180-191). q, k, v
+    are [B, N, H, D] with contiguous [H, D] rows (k / v may be row slices of kept-prefix buffers)."""
+
+    if src.stride(-1) != 1 or src.stride(-2) != src.shape[-1] or src.stride(-3) != src.shape[-1] * src.shape[-2]:
+        raise _lib.TfbError("rms_rope_qkv: src must be [B, N, 3, H, D] with contiguous (3, H, D) rows")
+    for t in (q, k, v):
+        if t.stride(-1) != 1 or t.stride(-2) != t.shape[-1]:
+            raise _lib.TfbError("rms_rope_qkv: destinations need contiguous [H, D] rows")
+    f = lambda t: t.float().contiguous()   # noqa: E731
+    _lib.rms_rope_qkv(src, f(wq), f(wk), f(cos), f(sin), eps, q, k, v)
+
+
 def swiglu(gu: torch.Tensor) -> torch.Tensor:
     """kernels.py:84-92: [M, 2F] = [gate | up] bf16 -> silu(gate) * up, [M, F] bf16."""
 

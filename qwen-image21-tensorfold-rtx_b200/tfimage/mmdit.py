@@ -149,9 +149,12 @@ class SynthMMDiT:
 
     @staticmethod
     def _mod(temb: torch.Tensor, w: torch.Tensor):
-        """-> (shift1, scale1, gate1, shift2, scale2, gate2), each [B, 1, dim]; gates tanh'ed (qwen_image21.py:272)."""
+        """-> (shift1, scale1, gate1, shift2, scale2, gate2), each [B, 1, dim]; gates tanh'ed (qwen_image21.py:272).
+        Shifts and scales are handed out as fp32 (exact copies of the bf16 values, the AdaLN kernel's input type),
+        once per forward rather than converted in each of the 56 AdaLN calls; gates stay bf16."""
         m = F.linear(F.silu(temb), w).unsqueeze(1).chunk(6, dim=-1)
-        return m[0], m[1], m[2].tanh(), m[3], m[4], m[5].tanh()
+        f = lambda t: t.float().contiguous()     # noqa: E731
+        return f(m[0]), f(m[1]), m[2].tanh(), f(m[3]), f(m[4]), m[5].tanh()
 
     def _block(self, b: Block, x, mod, cos, sin, kbuf, vbuf, causal=False, record: dict | None = None):
         """One block on rows x [B, N, dim] (in place); k / v are written to kbuf / vbuf [B, P + N, H, D] rows P:.
@@ -170,9 +173,7 @@ class SynthMMDiT:
             a_in = a_in.reshape(B * N, -1)
         qkv = b.qkv(a_in).view(B, N, 3, H, Dh)
         q = torch.empty((B, N, H, Dh), dtype=torch.bfloat16, device=x.device)
-        K.rms_rope(qkv, 0, b.norm_q, cos, sin, eps, q)
-        K.rms_rope(qkv, 1, b.norm_k, cos, sin, eps, kbuf[:, P:])
-        vbuf[:, P:].copy_(qkv[:, :, 2])
+        K.rms_rope_qkv(qkv, b.norm_q, b.norm_k, cos, sin, eps, q, kbuf[:, P:], vbuf[:, P:])
         o = _sdpa(q.transpose(1, 2), kbuf.transpose(1, 2), vbuf.transpose(1, 2), causal)
         o = o.transpose(1, 2)
         if rec:                       # the branch output on its own, then torch's addcmul_ (tests)

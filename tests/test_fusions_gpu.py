@@ -17,7 +17,8 @@ def within_ulp(y, ref, n=1, atol=1e-7):
     return (np.abs(y - ref) <= n * ulp_bf16(ref) + atol).all()
 
 
-@pytest.mark.parametrize("B,N,D", [(2, 37, 256), (1, 4352, 3072), (2, 300, 4096)])
+@pytest.mark.parametrize("B,N,D", [(2, 37, 256), (1, 4352, 3072), (2, 300, 4096), (2, 64, 512), (3, 50, 768),
+                                   (1, 129, 1536), (1, 40, 8192)])
 def test_adaln_matches_oracle(dev, B, N, D):
     x = bf16_cpu((B, N, D), seed=N, scale=3)
     g = torch.Generator().manual_seed(D)
@@ -38,10 +39,11 @@ def test_adaln_reference_fixture(dev):
         assert within_ulp(f32(y), ref)
 
 
-def test_adaln_fused_quant_bit_exact(dev):
+@pytest.mark.parametrize("N,D", [(4352 - 5, 3072), (300, 768)])
+def test_adaln_fused_quant_bit_exact(dev, N, D):
     """AdaLN(+shift) then NVFP4 quantize, in one pass; codes/scales equal the oracle quantizer applied
     to the kernel's own bf16 result (and padded scale rows are zero)."""
-    B, N, D = 1, 4352 - 5, 3072
+    B = 1
     x = bf16_cpu((B, N, D), seed=61)
     g = torch.Generator().manual_seed(62)
     s, sh = torch.randn(B, 1, D, generator=g) * 0.1, torch.randn(B, 1, D, generator=g) * 0.1
@@ -101,3 +103,27 @@ def test_swiglu_matches_oracle(dev, M, F):
     ref = ofu.swiglu(gu.float().numpy())
     assert (y == ref).mean() > 0.99
     assert within_ulp(y, ref, n=2)
+
+
+@pytest.mark.parametrize("B,N,H", [(1, 4352, 24), (2, 77, 3)])
+def test_rms_rope_qkv_matches_per_part_kernel(dev, B, N, H):
+    """tfb_rms_rope_qkv (q, k and the v copy in one pass) equals rms_rope per part bit for bit, writes k / v behind a
+    kept prefix without touching it, and v is the exact copy."""
+    D, P = 128, 5
+    qkv = bf16_cpu((B, N, 3, H, D), seed=N + 3).to(dev)
+    g = torch.Generator().manual_seed(72)
+    wq, wk = (torch.randn(D, generator=g) * 0.05 + 1).to(dev), (torch.randn(D, generator=g) * 0.05 + 1).to(dev)
+    cos, sin = ofu.rope_table(np.concatenate([ofu.text_ids(P), ofu.image_ids(1, N, P, (1, N))])[P:])
+    cs, sn = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    q_ref = torch.empty((B, N, H, D), dtype=torch.bfloat16, device=dev)
+    k_ref = torch.empty_like(q_ref)
+    K.rms_rope(qkv, 0, wq, cs, sn, 1e-6, q_ref)
+    K.rms_rope(qkv, 1, wk, cs, sn, 1e-6, k_ref)
+    q = torch.empty_like(q_ref)
+    kbuf = torch.full((B, P + N, H, D), 7.0, dtype=torch.bfloat16, device=dev)
+    vbuf = torch.full_like(kbuf, -3.0)
+    K.rms_rope_qkv(qkv, wq, wk, cs, sn, 1e-6, q, kbuf[:, P:], vbuf[:, P:])
+    torch.cuda.synchronize()
+    assert torch.equal(q, q_ref) and torch.equal(kbuf[:, P:], k_ref)
+    assert torch.equal(vbuf[:, P:], qkv[:, :, 2])
+    assert bool((kbuf[:, :P] == 7.0).all()) and bool((vbuf[:, :P] == -3.0).all())
