@@ -42,19 +42,28 @@ WORKLOAD = ("configs[1] fused NVFP4 MLP pair: X bf16 [4352,3072] N(0,1) -> gate/
             "SwiGLU->NVFP4 epilogue -> down W [3072,8192] N(0,0.02) -> bf16 [4352,3072]")
 
 
-def fp4_issue_peak():
-    """Dense FP4 MMA ceiling measured live by csrc/mma_peak_probe.cu (built by build.py --probe), or None."""
+def issue_peaks():
+    """Dense FP4 and FP8 MMA ceilings measured live by csrc/mma_peak_probe.cu (built by build.py --probe):
+    {"fp4": (TFLOP/s, cycles per MMA), "fp8": (...)}; missing entries when the probe is absent."""
     import re
     import subprocess
     exe = ROOT / "qwen-image21-tensorfold-rtx_b200" / "_build" / "mma_peak_probe"
     if not exe.exists():
-        return None
+        return {}
     try:
         out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60).stdout
-        m = re.search(r"mxf4nvf4.*?([0-9.]+) cycles/MMA\s+([0-9.]+) TFLOP/s", out)
-        return (float(m.group(2)), float(m.group(1))) if m else None
     except (OSError, subprocess.SubprocessError):
-        return None
+        return {}
+    found = {}
+    for key, pat in (("fp4", r"mxf4nvf4"), ("fp8", r"f8f6f4")):
+        m = re.search(pat + r".*?([0-9.]+) cycles/MMA\s+([0-9.]+) TFLOP/s", out)
+        if m:
+            found[key] = (float(m.group(2)), float(m.group(1)))
+    return found
+
+
+def fp4_issue_peak():
+    return issue_peaks().get("fp4")
 
 
 def peaks():
@@ -206,6 +215,113 @@ def run_reference(args):
                                        f"path restated in oracle/)"},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------- configs[0], [2], [3] legs
+def config_legs(dev, fp4_peak: float, fp8_peak: float, hbm_gbs: float) -> dict:
+    """The other BASELINE configs measured beside the headline: each kernel timed alone with CUDA events on the
+    launching stream, L2 flushed (256 MiB write) before every iteration, median of 20 after 3 warm-up runs."""
+    import numpy as np
+    import torch
+
+    from tfimage import _lib
+    from tfimage import kernels as Kn
+    from tfimage import linear as L
+    from tfimage import mmdit
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, it=20):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(it):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts) * 1e3                         # us
+
+    def act_input(m, k, seed):
+        g = torch.Generator().manual_seed(seed)
+        x = torch.randn(m, k, generator=g)
+        x[:, torch.randperm(k, generator=g)[:8]] *= 20             # 8 outlier channels x20
+        return x.to(torch.bfloat16).to(dev)
+
+    out = {}
+    # configs[0]: one NVFP4 W4A4 linear, X [4096, 3072], W [3072, 3072]
+    M0, K0 = 4096, 3072
+    x0 = act_input(M0, K0, 21)
+    g = torch.Generator().manual_seed(22)
+    lin = L.Nvfp4Linear((torch.randn(K0, K0, generator=g) * 0.02).to(torch.bfloat16).to(dev))
+    lin.set_act(float(_lib.absmax(x0)) / (6 * 448))
+    q0 = lin.quantize(x0)
+    t_gemm, t_quant = timed(lambda: lin(q0)), timed(lambda: lin.quantize(x0))
+    flop0 = 2 * M0 * K0 * K0
+    qbytes = M0 * K0 * 2 + M0 * K0 // 2 + M0 * K0 // 16
+    out["configs[0]"] = {
+        "workload": "NVFP4 W4A4 linear: X bf16 [4096, 3072] N(0,1), 8 channels x20; W [3072, 3072] N(0, 0.02)",
+        "gemm_us": t_gemm, "gemm_tflops": flop0 / t_gemm / 1e6, "gemm_frac_fp4_peak": flop0 / t_gemm / 1e6 / fp4_peak,
+        "quant_us": t_quant, "quant_gbs": qbytes / t_quant / 1e3, "quant_frac_hbm": qbytes / t_quant / 1e3 / hbm_gbs,
+        "linear_tflops": flop0 / (t_gemm + t_quant) / 1e6}
+    del x0, lin, q0
+
+    # configs[2]: AdaLN(+shift) + NVFP4 quantize on x [4352, 3072]; RMSNorm + RoPE of q, k (+ v) from qkv
+    M2, D = 4352, 3072
+    g = torch.Generator().manual_seed(23)
+    x2 = torch.randn(1, M2, D, generator=g).to(torch.bfloat16).to(dev)
+    sc = (torch.randn(1, 1, D, generator=g) * 0.1).to(dev)
+    sh = (torch.randn(1, 1, D, generator=g) * 0.1).to(dev)
+    t_ada = timed(lambda: Kn.adaln(x2, sc, 1e-6, shift=sh, quant=0.004))
+    ada_bytes = M2 * D * 2 + M2 * D // 2 + M2 * D // 16
+    H, Dh = 24, 128
+    qkv = torch.randn(1, M2, 3, H, Dh, generator=g).to(torch.bfloat16).to(dev)
+    wq = (torch.randn(Dh, generator=g) * 0.05 + 1).to(dev)
+    wk = (torch.randn(Dh, generator=g) * 0.05 + 1).to(dev)
+    cfg = mmdit.DitConfig()
+    ids = torch.cat([mmdit.text_ids(256, dev), mmdit.image_ids(64, 64, 256, dev)])
+    cos, sin = mmdit.rope_table(ids, cfg)
+    q = torch.empty(1, M2, H, Dh, dtype=torch.bfloat16, device=dev)
+    kb = torch.empty(1, M2 + 256, H, Dh, dtype=torch.bfloat16, device=dev)
+    vb = torch.empty_like(kb)
+    t_qkv = timed(lambda: Kn.rms_rope_qkv(qkv, wq, wk, cos, sin, 1e-6, q, kb[:, 256:], vb[:, 256:]))
+    t_qk = timed(lambda: (Kn.rms_rope(qkv, 0, wq, cos, sin, 1e-6, q), Kn.rms_rope(qkv, 1, wk, cos, sin, 1e-6, kb[:, 256:])))
+    plane = M2 * H * Dh * 2
+    rope_bytes = M2 * 64 * 8
+    out["configs[2]"] = {
+        "workload": "AdaLN(+shift)+NVFP4 quantize on x bf16 [4352, 3072] N(0,1), shift/scale N(0, 0.1); RMSNorm(q, k) "
+                    "+ 3-axis RoPE (16/56/56, 64x64 grid + 256 text ids) from qkv [4352, 3, 24, 128] N(0,1)",
+        "adaln_quant_us": t_ada, "adaln_quant_gbs": ada_bytes / t_ada / 1e3,
+        "adaln_quant_frac_hbm": ada_bytes / t_ada / 1e3 / hbm_gbs,
+        "rms_rope_qkv_us": t_qkv, "rms_rope_qkv_gbs": (6 * plane + rope_bytes) / t_qkv / 1e3,
+        "rms_rope_qkv_frac_hbm": (6 * plane + rope_bytes) / t_qkv / 1e3 / hbm_gbs,
+        "rms_rope_q_k_us": t_qk, "rms_rope_q_k_gbs": (4 * plane + 2 * rope_bytes) / t_qk / 1e3,
+        "bytes": {"adaln_quant": ada_bytes, "rms_rope_qkv": 6 * plane + rope_bytes,
+                  "rms_rope_q_k": 4 * plane + 2 * rope_bytes}}
+    del x2, qkv, q, kb, vb
+
+    # configs[3]: FP8 W8A8, per-tensor activation scale, per-channel weight scales, ragged M = 4968
+    M3 = 4968
+    x3 = act_input(M3, 3072, 24)
+    res = {"workload": "FP8 E4M3 W8A8, per-tensor act / per-channel W scales, M = 4968 (4712 image + 256 text)"}
+    for name, n, k in (("linear_3072", 3072, 3072), ("gate_up_16384", 16384, 3072), ("down_3072_k8192", 3072, 8192)):
+        g = torch.Generator().manual_seed(n + k)
+        f8 = L.Fp8Linear((torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16).to(dev), per_channel=True)
+        xin = x3 if k == 3072 else act_input(M3, k, 25)
+        a = _lib.fp8_act_scale(xin)
+        q8 = _lib.quant_fp8(xin, a)
+        t8 = timed(lambda: _lib.gemm_fp8(q8, f8.w8.view(torch.uint8), M3, n, k, a, f8.ws))
+        fl = 2 * M3 * n * k
+        res[name] = {"gemm_us": t8, "tflops": fl / t8 / 1e6, "frac_fp8_peak": fl / t8 / 1e6 / fp8_peak}
+    out["configs[3]"] = res
+    out["peaks"] = {"fp4_tflops": fp4_peak, "fp8_tflops": fp8_peak, "hbm_gbs": hbm_gbs}
+    del flush
+    _ = np
+    return out
 
 
 # ------------------------------------------------------------------------------------------------- DiT leg
@@ -376,7 +492,8 @@ def run_ours(args):
     if rank == 0:
         pk, src = peaks()
         derived = FP4_TO_BF16 * pk["bf16_tflops"]
-        probe = fp4_issue_peak()
+        probes = issue_peaks()
+        probe = probes.get("fp4")
         if probe:
             fp4_peak = probe[0]
             peak_note = (f"measured: tcgen05 mxf4nvf4 M128xN256xK64 issue-rate probe, {probe[1]:.1f} cycles/MMA, "
@@ -409,6 +526,11 @@ def run_ours(args):
             "device_status": status,
             "dit": dit,
         }
+        if not args.no_configs:
+            fp8_peak = probes["fp8"][0] if "fp8" in probes else 2 * pk["bf16_tflops"]
+            line["configs"] = config_legs(dev, fp4_peak, fp8_peak, pk["hbm_gbs"])
+            line["configs"]["peaks"]["source"] = ("tcgen05 issue-rate probe (csrc/mma_peak_probe.cu); HBM: "
+                                                  f"MEASURED_PEAKS.json copy ({src})")
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
@@ -425,6 +547,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-dit", action="store_true", help="skip the configs[4] DiT leg (latency + img/s)")
+    ap.add_argument("--no-configs", action="store_true", help="skip the configs[0], [2], [3] kernel lines")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
