@@ -365,6 +365,25 @@ def dit_leg(world: int, rank: int, dev, barrier, reduce_max) -> dict:
     barrier()
     step_ms = reduce_max(statistics.median(a.elapsed_time(b) for a, b in lat))
 
+    # single-image latency with the MLP split over the ranks (NCCL all-reduce of the bf16 down partial per block)
+    tp_lat = None
+    if world > 1:
+        model.enable_tp()
+        for _ in range(3):
+            model.forward(x1, t1, prefix, work)
+        barrier()
+        lat = [(ev(), ev()) for _ in range(10)]
+        for a, b in lat:
+            a.record(stream)
+            model.forward(x1, t1, prefix, work)
+            b.record(stream)
+        barrier()
+        tp_lat = {"world": world, "step_ms": reduce_max(statistics.median(a.elapsed_time(b) for a, b in lat)),
+                  "split": "MLP: gate/up columns (pairs kept local) and down rows over the ranks; attention, qkv, "
+                           "out replicated",
+                  "collective": "NCCL all-reduce (sum) of the bf16 down partial [4096, 3072] per block"}
+        model.disable_tp()
+
     # throughput: this rank's seeds through the whole sampler, the prompt's prefix built inside the timed region
     model.forward(noise.to(torch.bfloat16), torch.full((counts[rank],), 0.5, device=dev), prefix, {})
     barrier()
@@ -382,7 +401,7 @@ def dit_leg(world: int, rank: int, dev, barrier, reduce_max) -> dict:
             "seeds_per_rank": counts, "steps": DIT_STEPS, "scaling": "strong (32 seeds split across ranks)",
             "parallelism": f"dp{world} (weight replica per rank, no collective)",
             "weights_gb": model.nbytes() / 1e9, "launches_per_step": 9 * model.cfg.layers + 1,
-            "tensor_parallel_latency": None, "finite": ok, "clocks": clk.report(),
+            "tensor_parallel_latency": tp_lat, "finite": ok, "clocks": clk.report(),
             "timing": "CUDA events on the launching stream, max over ranks; latency = median of 10 steps after 3 "
                       "warm-up; throughput = one timed 25-step sampler run (prefix included) after a warm-up step"}
 

@@ -24,7 +24,7 @@
 //                   stores crowd the memory-instruction path the MMA issue shares and stalled it ~4500 cycles/tile.
 // Every mbarrier wait is bounded (kWaitLimitNs); a wait that runs out records a code in the device error word,
 // the other roles see it and leave their loops, in-flight copies/MMAs are drained (bounded) and TMEM is freed.
-// No TMA multicast anywhere: each CTA loads its own operand tiles.
+// Each CTA issues its own tile loads from this GPU's memory; no load is broadcast across the cluster.
 #include <stdlib.h>
 
 #include <atomic>

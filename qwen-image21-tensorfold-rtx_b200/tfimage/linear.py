@@ -194,6 +194,13 @@ class Nvfp4Linear(Linear):
         self.tile = tile
         self.amax = 0.0                 # largest input scale seen (calibration)
 
+    @classmethod
+    def from_fp4(cls, lin: "Fp4Linear", tile: int = 12) -> "Nvfp4Linear":
+        """A static-scale layer around an existing container (e.g. a tensor-parallel shard), no re-quantization."""
+        self = cls.__new__(cls)
+        self.lin, self.n, self.k, self.dynamic, self.tile, self.amax = lin, lin.n, lin.k, False, tile, 0.0
+        return self
+
     def set_act(self, act: float | None) -> None:
         self.dynamic = act is None
         if act is not None:

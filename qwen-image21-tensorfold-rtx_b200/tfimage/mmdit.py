@@ -87,6 +87,7 @@ class Block:
     down: L.Linear
     norm_q: torch.Tensor       # fp32 [head_dim]
     norm_k: torch.Tensor
+    tp: object = None          # tp.TPMLP: this rank's MLP shard (single-image latency mode)
 
 
 @dataclass
@@ -186,6 +187,9 @@ class SynthMMDiT:
         m_in = K.adaln(x, sc2, eps, shift=sh2, quant=b.gate_up if static else None, out=bf() if static else None)
         if rec:
             x1 = x.clone()
+        if b.tp is not None and static and not rec:
+            b.tp(m_in, residual=(x, g2))   # this rank's MLP shard, NCCL all-reduce, then the gated residual
+            return x
         if static and not rec and L.swiglu_mlp(b.gate_up, b.down, m_in, residual=(x, g2)) is not None:
             return x                  # x += g2 * down(SwiGLU(gate_up(m))), in the down GEMM's epilogue
         y = L.swiglu_mlp(b.gate_up, b.down, m_in) if static else None
@@ -258,6 +262,18 @@ class SynthMMDiT:
             if step_events is not None:
                 step_events[i].record()
         return x
+
+    def enable_tp(self, group=None) -> None:
+        """Single-image latency mode: split every image block's MLP over the ranks of ``group`` (gate/up columns,
+        down rows; tp.TPMLP), attention and the other linears replicated. Needs calibrated (static) scales."""
+        from .tp import TPMLP
+
+        for b in self.img_blocks:
+            b.tp = TPMLP(b.gate_up, b.down, group)
+
+    def disable_tp(self) -> None:
+        for b in self.img_blocks:
+            b.tp = None
 
     # ------------------------------------------------------------------------------------------- calibration
     @torch.inference_mode()
