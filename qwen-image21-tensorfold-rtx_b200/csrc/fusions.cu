@@ -224,7 +224,11 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __rest
   unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(gu + m * 2 * F + F + c)), u);
   float y[8];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) y[k] = bf16_round(__fdiv_rn(g[k], 1.0f + expf(-g[k]))) * u[k];
+  for (int k = 0; k < 8; k += 2) {   // silu rounded to bf16 two at a time (one paired conversion)
+    const uint32_t sp = pack_bf16x2(__fdiv_rn(g[k], 1.0f + expf(-g[k])), __fdiv_rn(g[k + 1], 1.0f + expf(-g[k + 1])));
+    y[k] = __uint_as_float(sp << 16) * u[k];
+    y[k + 1] = __uint_as_float(sp & 0xFFFF0000u) * u[k + 1];
+  }
   *reinterpret_cast<uint4*>(out + m * F + c) =
       make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
 }
