@@ -27,6 +27,8 @@ __global__ void __launch_bounds__(kAdaThreads) adaln_kernel(const __nv_bfloat16*
                                                             const float* __restrict__ shift, float eps,
                                                             __nv_bfloat16* __restrict__ out, float qg,
                                                             uint8_t* __restrict__ codes, uint8_t* __restrict__ sf) {
+  pdl_trigger();
+  pdl_wait();
   using S = AdaSplit<NCH>;
   constexpr int D = NCH * 256, WPR = S::WPR, CPT = S::CPT, RPB = S::RPB;
   __shared__ float red[2][RPB][WPR];
@@ -130,7 +132,7 @@ void launch_adaln(const void* x, int64_t rows, int64_t rows_total, int64_t rows_
                   const float* shift, float eps, void* out, float qg, uint8_t* codes, uint8_t* sf, cudaStream_t s) {
   constexpr int RPB = AdaSplit<NCH>::RPB;
   const int64_t grid = (rows_total + RPB - 1) / RPB;
-  adaln_kernel<NCH><<<grid, kAdaThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, rows_total, rows_per_b,
+  TFB_LAUNCH(adaln_kernel<NCH>, grid, kAdaThreads, s, static_cast<const __nv_bfloat16*>(x), rows, rows_total, rows_per_b,
                                                  scale, shift, eps, static_cast<__nv_bfloat16*>(out), qg, codes, sf);
 }
 
@@ -166,6 +168,8 @@ __global__ void __launch_bounds__(256) rms_rope_kernel(const __nv_bfloat16* __re
                                                        const float* __restrict__ sinp, float eps,
                                                        __nv_bfloat16* __restrict__ dst, int64_t dst_sb,
                                                        int64_t dst_sn) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int D = 128;
   const int64_t unit = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 4;
   const int l = threadIdx.x & 15;
@@ -188,6 +192,8 @@ __global__ void __launch_bounds__(256) rms_rope_qkv_kernel(
     const float* __restrict__ sinp, float eps, __nv_bfloat16* __restrict__ qd, int64_t q_sb, int64_t q_sn,
     __nv_bfloat16* __restrict__ kd, int64_t k_sb, int64_t k_sn, __nv_bfloat16* __restrict__ vd, int64_t v_sb,
     int64_t v_sn) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int D = 128;
   const int64_t unit = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 4;
   const int l = threadIdx.x & 15;
@@ -215,6 +221,8 @@ __global__ void __launch_bounds__(256) rms_rope_qkv_kernel(
 // bf16(bf16(silu(g)) * u), 8 columns per thread.
 __global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __restrict__ gu, int64_t M, int64_t F,
                                                      __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t per_row = F >> 3;
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (t >= M * per_row) return;
@@ -283,7 +291,7 @@ tfb_status tfb_rms_rope(const void* src, int64_t B, int64_t N, int64_t H, int64_
   const int64_t units = B * N * H;
   if (units == 0) return TFB_OK;
   const int64_t threads = units * 16;
-  rms_rope_kernel<<<(threads + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  TFB_LAUNCH(rms_rope_kernel, (threads + 255) / 256, 256, static_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(src), units, N, H, src_sb, src_sn, src_off, w, cos, sin, eps,
       static_cast<__nv_bfloat16*>(dst), dst_sb, dst_sn);
   TFB_CUDA(cudaGetLastError());
@@ -306,7 +314,7 @@ tfb_status tfb_rms_rope_qkv(const void* src, int64_t B, int64_t N, int64_t H, in
   const int64_t units = B * N * H;
   if (units == 0) return TFB_OK;
   const int64_t threads = units * 16;
-  rms_rope_qkv_kernel<<<(threads + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  TFB_LAUNCH(rms_rope_qkv_kernel, (threads + 255) / 256, 256, static_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(src), units, N, H, src_sb, src_sn, wq, wk, cos, sin, eps,
       static_cast<__nv_bfloat16*>(q), q_sb, q_sn, static_cast<__nv_bfloat16*>(k), k_sb, k_sn,
       static_cast<__nv_bfloat16*>(v), v_sb, v_sn);
@@ -323,7 +331,7 @@ tfb_status tfb_swiglu(const void* gu, int64_t M, int64_t F, void* out, void* str
   if (!aligned(gu, 16) || !aligned(out, 16)) return fail(TFB_BAD_ALIGN, "swiglu: buffers must be 16-byte aligned");
   const int64_t threads = M * (F / 8);
   if (threads == 0) return TFB_OK;
-  swiglu_kernel<<<(threads + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  TFB_LAUNCH(swiglu_kernel, (threads + 255) / 256, 256, static_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(gu), M, F, static_cast<__nv_bfloat16*>(out));
   TFB_CUDA(cudaGetLastError());
   return TFB_OK;

@@ -473,6 +473,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
   }
   tc_fence_after();
+  // everything above (barriers, TMEM) overlapped the previous kernel's tail; its outputs are read only below
+  pdl_trigger();
+  pdl_wait();
   const uint32_t tmem = *tmem_slot;
   // the leader's copies of `ready` and `acc_empty`, as shared::cluster addresses
   uint32_t ready_l = smem_u32(ready), acc_empty_l = smem_u32(acc_empty), full_l = smem_u32(full);
@@ -932,13 +935,15 @@ tfb_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = Cfg<MODE, CG>::SMEM;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = CG;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // pdl_trigger / pdl_wait in the kernel
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = CG;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = CG == 2 ? 1 : 0;
+  cfg.numAttrs = CG == 2 ? 2 : 1;
   // Persistent grid: as many groups as can be resident at once. A CTA pair must sit inside one GPC, so on parts
   // whose GPCs hold an odd number of usable SMs fewer than sm_count / 2 pairs fit; a larger grid would run its
   // extra pairs as a second wave after the first ones finished all their tiles.

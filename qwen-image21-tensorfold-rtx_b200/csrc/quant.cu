@@ -10,6 +10,8 @@ constexpr int kThreads = 256;
 __global__ void __launch_bounds__(kThreads) absmax_kernel(const uint4* __restrict__ x, int64_t nvec,
                                                          const __nv_bfloat16* __restrict__ tail, int ntail,
                                                          unsigned int* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   float m = 0.0f;
   for (int64_t i = blockIdx.x * (int64_t)kThreads + threadIdx.x; i < nvec; i += (int64_t)gridDim.x * kThreads) {
     float f[8];
@@ -30,7 +32,11 @@ __global__ void __launch_bounds__(kThreads) absmax_kernel(const uint4* __restric
 }
 
 // a = max(amax / 448, 1e-12) (tfimage/linear.py:86)
-__global__ void fp8_scale_finalize(float* a) { *a = fmaxf(__fdiv_rn(*a, 448.0f), 1e-12f); }
+__global__ void fp8_scale_finalize(float* a) {
+  pdl_trigger();
+  pdl_wait();
+  *a = fmaxf(__fdiv_rn(*a, 448.0f), 1e-12f);
+}
 
 tfb_status launch_absmax(const void* x, int64_t n, float* out, cudaStream_t s) {
   const DeviceInfo* di;
@@ -43,7 +49,7 @@ tfb_status launch_absmax(const void* x, int64_t n, float* out, cudaStream_t s) {
   int ntail = static_cast<int>(n - nvec * 8);
   int64_t want = (nvec + kThreads - 1) / kThreads;
   int grid = static_cast<int>(want < (int64_t)di->sm_count * 8 ? (want > 0 ? want : 1) : (int64_t)di->sm_count * 8);
-  absmax_kernel<<<grid, kThreads, 0, s>>>(static_cast<const uint4*>(x), nvec,
+  TFB_LAUNCH(absmax_kernel, grid, kThreads, s, static_cast<const uint4*>(x), nvec,
                                           static_cast<const __nv_bfloat16*>(x) + nvec * 8, ntail,
                                           reinterpret_cast<unsigned int*>(out));
   TFB_CUDA(cudaGetLastError());
@@ -57,6 +63,8 @@ template <bool TILED>
 __global__ void __launch_bounds__(kThreads) quant_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, int64_t M,
                                                               int64_t rows_total, int64_t K, int64_t ldx, float g,
                                                               uint8_t* __restrict__ codes, uint8_t* __restrict__ sf) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t nb = K >> 4;
   const int64_t blk = blockIdx.x * (int64_t)kThreads + threadIdx.x;
   const int64_t row = blk / nb, j = blk - row * nb;
@@ -97,6 +105,8 @@ __global__ void __launch_bounds__(kThreads) quant_nvfp4_kernel(const __nv_bfloat
 __global__ void __launch_bounds__(kThreads) quant_fp8_kernel(const __nv_bfloat16* __restrict__ x, int64_t M, int64_t K,
                                                             int64_t ldx, const float* __restrict__ a_dev,
                                                             uint8_t* __restrict__ q) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t nb = K >> 4;
   const int64_t blk = blockIdx.x * (int64_t)kThreads + threadIdx.x;
   const int64_t row = blk / nb, j = blk - row * nb;
@@ -140,10 +150,10 @@ tfb_status quant_nvfp4(const void* x, int64_t M, int64_t K, int64_t ldx, float g
   if (blocks == 0) return TFB_OK;
   const int64_t grid = (blocks + kThreads - 1) / kThreads;
   if (layout == TFB_SF_TILED)
-    quant_nvfp4_kernel<true><<<grid, kThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(x), M, rows_total, K, ldx,
+    TFB_LAUNCH(quant_nvfp4_kernel<true>, grid, kThreads, s, static_cast<const __nv_bfloat16*>(x), M, rows_total, K, ldx,
                                                        g, codes, sf);
   else
-    quant_nvfp4_kernel<false><<<grid, kThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(x), M, rows_total, K, ldx,
+    TFB_LAUNCH(quant_nvfp4_kernel<false>, grid, kThreads, s, static_cast<const __nv_bfloat16*>(x), M, rows_total, K, ldx,
                                                         g, codes, sf);
   TFB_CUDA(cudaGetLastError());
   return TFB_OK;
@@ -161,7 +171,7 @@ tfb_status tfb_fp8_act_scale(const void* x, int64_t n, float* a_dev, void* strea
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   tfb_status st = tfb::launch_absmax(x, n, a_dev, s);
   if (st != TFB_OK) return st;
-  tfb::fp8_scale_finalize<<<1, 1, 0, s>>>(a_dev);
+  TFB_LAUNCH(tfb::fp8_scale_finalize, 1, 1, s, a_dev);
   TFB_CUDA(cudaGetLastError());
   return TFB_OK;
 }
@@ -182,7 +192,7 @@ tfb_status tfb_quant_fp8(const void* x, int64_t M, int64_t K, int64_t ldx, const
     return tfb::fail(TFB_BAD_ALIGN, "quant_fp8: x, ldx and q must be 16-byte aligned");
   const int64_t blocks = M * (K / 16);
   if (blocks == 0) return TFB_OK;
-  tfb::quant_fp8_kernel<<<(blocks + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  TFB_LAUNCH(tfb::quant_fp8_kernel, (blocks + 255) / 256, 256, static_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(x), M, K, ldx, a_dev, q);
   TFB_CUDA(cudaGetLastError());
   return TFB_OK;

@@ -39,6 +39,25 @@ tfb_status make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint
                         uint64_t row_stride, uint32_t box_inner, uint32_t box_rows, bool swizzle);
 
 // NVFP4 row quantizer launch (quant.cu); shared by the fused MLP entry point.
+// Launch with programmatic stream serialization (see pdl_trigger / pdl_wait). Launch errors are picked up by the
+// cudaGetLastError() check that follows every launch site.
+#define TFB_LAUNCH(kernel, grid, block, stream, ...) \
+  (void)::tfb::launch_pdl(kernel, dim3(grid), dim3(block), 0, stream, __VA_ARGS__)
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 tfb_status quant_nvfp4(const void* x, int64_t M, int64_t K, int64_t ldx, float g, uint8_t* codes, uint8_t* sf,
                        int layout, cudaStream_t s);
 
@@ -109,6 +128,14 @@ __device__ __forceinline__ uint32_t nvfp4_codes8(const float* x, float inv) {
 __device__ __forceinline__ size_t sf_tiled_offset(int64_t row, int64_t j, int64_t chunks) {
   return (static_cast<size_t>(row >> 7) * chunks + (j >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4 + (j & 3);
 }
+
+// Programmatic dependent launch. Every kernel of the library is launched with programmatic stream serialization,
+// lets the next kernel launch as soon as all of its own CTAs are running (pdl_trigger), and waits for the previous
+// kernel of the stream to complete -- with its memory visible -- before its first read of anything that kernel may
+// have written (pdl_wait). What runs before pdl_wait (barrier set-up, TMEM allocation, tensor-map prefetch) overlaps
+// the previous kernel's tail. Without a programmatic predecessor both are no-ops.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
