@@ -278,6 +278,70 @@ def swiglu_mlp(gate_up: Linear, down: Linear, x: torch.Tensor, residual=None):
     return down(h, residual=residual)
 
 
+_COPY_STREAMS: dict = {}
+_HOST_GRAPHS: dict = {}
+
+
+def _mlp_host_pipeline(gate_up, down, x_host, y_host, xd, chunks: int) -> bool:
+    dev = xd.device
+    if dev not in _COPY_STREAMS:
+        _COPY_STREAMS[dev] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    s_in, s_out = _COPY_STREAMS[dev]
+    cur = torch.cuda.current_stream(dev)
+    M = x_host.shape[0]
+    step = max(256, -(-M // chunks + 255) // 256 * 256)          # whole 256-row pair tiles per chunk
+    s_in.wait_stream(cur)
+    s_out.wait_stream(cur)
+    for r0 in range(0, M, step):
+        r1 = min(M, r0 + step)
+        with torch.cuda.stream(s_in):
+            xd[r0:r1].copy_(x_host[r0:r1], non_blocking=True)
+        cur.wait_stream(s_in)
+        y = swiglu_mlp(gate_up, down, xd[r0:r1])
+        if y is None:
+            return False
+        s_out.wait_stream(cur)
+        with torch.cuda.stream(s_out):
+            y_host[r0:r1].copy_(y, non_blocking=True)
+        y.record_stream(s_out)
+    cur.wait_stream(s_out)
+    return True
+
+
+def swiglu_mlp_host(gate_up: Linear, down: Linear, x_host: torch.Tensor, y_host: torch.Tensor, chunks: int = 3,
+                    graph: bool = False):
+    """This build's addition: ``swiglu_mlp`` on host-resident rows, pinned ``x_host`` [M, K] -> ``y_host`` [M, K],
+    with the PCIe copies overlapped. The rows go in ``chunks`` pieces: chunk i+1 is copied in while chunk i computes
+    and chunk i-1 is copied back, both directions of the link at once. Every op is row-wise, so the result equals one
+    ``swiglu_mlp`` call on the whole input. The current stream waits for the last copy (time it with events on it).
+
+    ``graph=True``: the pipeline for these layers, these two host buffers and this shape is captured into a CUDA
+    graph on the first call and replayed afterwards (no per-call host work; the caller keeps the buffers and
+    refills ``x_host`` in place). Without it each chunk costs three library calls of host time, which starves the
+    GPU beyond ~3 chunks. None if the layers cannot take the fused path."""
+    if not (isinstance(gate_up, Nvfp4Linear) and isinstance(down, Nvfp4Linear)) or gate_up.dynamic or down.dynamic:
+        return None
+    dev = gate_up.lin.words.device
+    if not graph:
+        xd = torch.empty(tuple(x_host.shape), dtype=torch.bfloat16, device=dev)
+        return y_host if _mlp_host_pipeline(gate_up, down, x_host, y_host, xd, chunks) else None
+    k = (id(gate_up), id(down), x_host.data_ptr(), y_host.data_ptr(), tuple(x_host.shape), chunks, dev)
+    entry = _HOST_GRAPHS.get(k)
+    if entry is None:
+        xd = torch.empty(tuple(x_host.shape), dtype=torch.bfloat16, device=dev)
+        if not _mlp_host_pipeline(gate_up, down, x_host, y_host, xd, chunks):   # warm-up: one-time set-up calls
+            return None
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side), torch.cuda.graph(g, stream=side):
+            _mlp_host_pipeline(gate_up, down, x_host, y_host, xd, chunks)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        entry = _HOST_GRAPHS[k] = (g, xd, gate_up, down)
+    entry[0].replay()
+    return y_host
+
+
 def make(kind: str, w: torch.Tensor, act: float | None = None) -> Linear:
     """linear.py:153-161: a backend by name for a bf16 [N, K] weight (dims the kernels cannot tile fall back to
     FP8, then bf16, as in the reference)."""

@@ -208,3 +208,28 @@ def test_swiglu_mlp_gated_residual(dev):
     out = res.clone()
     assert L.swiglu_mlp(gu, down, x.view(M, K), residual=(out, gate)) is out
     assert (f32(out) == f32(ref)).mean() >= 0.9999
+
+
+def test_swiglu_mlp_host_streams_rows_bit_identically(dev):
+    """swiglu_mlp_host (pinned rows in chunks, copies overlapped) equals one swiglu_mlp call on the device."""
+    M, K, F = 1000, 512, 384
+    gu = L.Nvfp4Linear(bf16_cpu((2 * F, K), seed=91, scale=0.05).to(dev), act=0.003)
+    down = L.Nvfp4Linear(bf16_cpu((K, F), seed=92, scale=0.05).to(dev), act=0.002)
+    x = bf16_cpu((M, K), seed=93)
+    ref = L.swiglu_mlp(gu, down, x.to(dev)).cpu()
+    xp = x.pin_memory()
+    for chunks, graph in ((1, False), (3, False), (8, False), (3, True), (8, True)):
+        y = torch.full((M, K), float("nan"), dtype=torch.bfloat16).pin_memory()
+        for _ in range(2 if graph else 1):       # graph: capture on the first call, replay on the second
+            y.fill_(float("nan"))
+            out = L.swiglu_mlp_host(gu, down, xp, y, chunks=chunks, graph=graph)
+            torch.cuda.synchronize()
+            assert out is y and torch.equal(y, ref), (chunks, graph)
+    # a replay reads the host buffer's current contents
+    x2 = bf16_cpu((M, K), seed=94)
+    xp.copy_(x2)
+    y = torch.empty((M, K), dtype=torch.bfloat16).pin_memory()
+    for _ in range(2):
+        L.swiglu_mlp_host(gu, down, xp, y, chunks=8, graph=True)
+    torch.cuda.synchronize()
+    assert torch.equal(y, L.swiglu_mlp(gu, down, x2.to(dev)).cpu())
