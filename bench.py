@@ -37,7 +37,7 @@ FLOP_STEP = FLOP_GU + FLOP_DOWN
 FP4_TO_BF16 = 4.0                                  # B200 dense FP4 : BF16 tensor rate (9 : 2.25 PFLOP/s)
 # DRAM bytes per gate/up launch (dram__bytes_read.sum + dram__bytes_write.sum) from the ncu capture summarised in
 # profiles/gemm_nvfp4_config1.md.
-TRAFFIC_GU = 37.24e6
+TRAFFIC_GU = 36.87e6
 WORKLOAD = ("configs[1] fused NVFP4 MLP pair: X bf16 [4352,3072] N(0,1) -> gate/up W [16384,3072] N(0,0.02) with "
             "SwiGLU->NVFP4 epilogue -> down W [3072,8192] N(0,0.02) -> bf16 [4352,3072]")
 
