@@ -354,16 +354,21 @@ def dit_leg(world: int, rank: int, dev, barrier, reduce_max) -> dict:
     x1 = noise[:1].to(torch.bfloat16)
     t1 = torch.full((1,), 0.5, device=dev)
     work: dict = {}
-    for _ in range(3):
-        model.forward(x1, t1, prefix, work)
-    barrier()
-    lat = [(ev(), ev()) for _ in range(10)]
-    for a, b in lat:
-        a.record(stream)
-        model.forward(x1, t1, prefix, work)
-        b.record(stream)
-    barrier()
-    step_ms = reduce_max(statistics.median(a.elapsed_time(b) for a, b in lat))
+
+    def latency(fn):
+        for _ in range(3):
+            fn()
+        barrier()
+        lat = [(ev(), ev()) for _ in range(10)]
+        for a, b in lat:
+            a.record(stream)
+            fn()
+            b.record(stream)
+        barrier()
+        return reduce_max(statistics.median(a.elapsed_time(b) for a, b in lat))
+
+    step_ms_eager = latency(lambda: model.forward(x1, t1, prefix, work))
+    step_ms = latency(lambda: model.step_graph(x1, t1, prefix))          # one captured forward per step
 
     # single-image latency with the MLP split over the ranks (NCCL all-reduce of the bf16 down partial per block)
     tp_lat = None
@@ -385,25 +390,28 @@ def dit_leg(world: int, rank: int, dev, barrier, reduce_max) -> dict:
         model.disable_tp()
 
     # throughput: this rank's seeds through the whole sampler, the prompt's prefix built inside the timed region
-    model.forward(noise.to(torch.bfloat16), torch.full((counts[rank],), 0.5, device=dev), prefix, {})
+    model.sample(noise, prefix, 1, graph=True)           # captures this batch's step graph (one-time)
     barrier()
     a, b = ev(), ev()
     with ClockSampler(dev.index) as clk:
         a.record(stream)
-        prefix = model.build_prefix(ctx)
-        lat_out = model.sample(noise, prefix, DIT_STEPS)
+        prefix = model.build_prefix(ctx, into=prefix)     # the prompt's prefix pass, into the graph's buffers
+        lat_out = model.sample(noise, prefix, DIT_STEPS, graph=True)
         b.record(stream)
         barrier()
     sample_s = reduce_max(a.elapsed_time(b)) / 1e3
     ok = bool(torch.isfinite(lat_out).all())
-    return {"workload": DIT_WORKLOAD, "step_ms_at_4096_tokens": step_ms, "step_batch": 1,
+    return {"workload": DIT_WORKLOAD, "step_ms_at_4096_tokens": step_ms, "step_ms_eager": step_ms_eager,
+            "step_batch": 1,
             "img_per_s": DIT_SEEDS / sample_s, "sample_s": sample_s, "seeds": DIT_SEEDS,
             "seeds_per_rank": counts, "steps": DIT_STEPS, "scaling": "strong (32 seeds split across ranks)",
             "parallelism": f"dp{world} (weight replica per rank, no collective)",
             "weights_gb": model.nbytes() / 1e9, "launches_per_step": 9 * model.cfg.layers + 1,
             "tensor_parallel_latency": tp_lat, "finite": ok, "clocks": clk.report(),
             "timing": "CUDA events on the launching stream, max over ranks; latency = median of 10 steps after 3 "
-                      "warm-up; throughput = one timed 25-step sampler run (prefix included) after a warm-up step"}
+                      "warm-up, each step one replayed CUDA graph of the forward (eager launches: step_ms_eager); "
+                      "throughput = one timed 25-step sampler run (graph steps, prefix pass included) after a "
+                      "warm-up step"}
 
 
 # ------------------------------------------------------------------------------------------------------ our arm

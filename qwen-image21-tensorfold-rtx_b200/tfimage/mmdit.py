@@ -203,8 +203,9 @@ class SynthMMDiT:
 
     # ------------------------------------------------------------------------------------------- prefix
     @torch.inference_mode()
-    def build_prefix(self, context: torch.Tensor) -> Prefix:
-        """context [1, L, txt_dim] -> the kept per-block text keys / values (t = 0 modulation, causal)."""
+    def build_prefix(self, context: torch.Tensor, into: Prefix | None = None) -> Prefix:
+        """context [1, L, txt_dim] -> the kept per-block text keys / values (t = 0 modulation, causal). ``into``: an
+        earlier prefix of the same length whose buffers are overwritten (captured step graphs keep using them)."""
         cfg = self.cfg
         c = context.to(self.device).float()
         c = c * torch.rsqrt(c.pow(2).mean(-1, keepdim=True) + cfg.eps) * self.txt_norm
@@ -213,13 +214,18 @@ class SynthMMDiT:
         B, P, _ = x.shape
         cos, sin = rope_table(text_ids(P, self.device), cfg)
         mod = self._mod(self._temb(torch.zeros((B,), device=self.device)), self.mod_txt)
+        if into is not None and (into.length != P or into.kv[0][0].shape[0] != B):
+            raise ValueError("build_prefix(into=...): the kept prefix has another length or batch")
         kv = []
-        for b in self.txt_blocks:
-            k = torch.empty((B, P, cfg.heads, cfg.head_dim), dtype=torch.bfloat16, device=self.device)
-            v = torch.empty_like(k)
+        for i, b in enumerate(self.txt_blocks):
+            if into is not None:
+                k, v = into.kv[i]
+            else:
+                k = torch.empty((B, P, cfg.heads, cfg.head_dim), dtype=torch.bfloat16, device=self.device)
+                v = torch.empty_like(k)
             x = self._block(b, x, mod, cos, sin, k, v, causal=True)
             kv.append((k, v))
-        return Prefix(kv, P, P)
+        return into if into is not None else Prefix(kv, P, P)
 
     # ------------------------------------------------------------------------------------------- step
     @torch.inference_mode()
@@ -250,14 +256,41 @@ class SynthMMDiT:
     __call__ = forward
 
     @torch.inference_mode()
-    def sample(self, noise: torch.Tensor, prefix: Prefix, steps: int = 25, step_events=None) -> torch.Tensor:
-        """Flow-matching Euler from unit-Gaussian noise [B, 64, H, W] (sampling.py:19-31)."""
+    def step_graph(self, x: torch.Tensor, t: torch.Tensor, prefix: Prefix) -> torch.Tensor:
+        """``forward`` replayed from a CUDA graph: the first call for a (shape, prefix) captures one forward with
+        static input / output buffers, later calls copy ``x`` and ``t`` in and replay it (no per-kernel host work,
+        no launch gaps). Returns the static output buffer: consume it before the next call."""
+        graphs = self.__dict__.setdefault("_graphs", {})
+        key = (tuple(x.shape), id(prefix))
+        entry = graphs.get(key)
+        if entry is None:
+            xs, ts, work = x.clone(), t.clone(), {}
+            self.forward(xs, ts, prefix, work)                   # warm-up: one-time set-up outside the capture
+            side = torch.cuda.Stream(x.device)
+            side.wait_stream(torch.cuda.current_stream(x.device))
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(side), torch.cuda.graph(g, stream=side):
+                out = self.forward(xs, ts, prefix, work)
+            torch.cuda.current_stream(x.device).wait_stream(side)
+            entry = graphs[key] = (g, xs, ts, out, work)
+        g, xs, ts, out, _ = entry
+        xs.copy_(x)
+        ts.copy_(t)
+        g.replay()
+        return out
+
+    @torch.inference_mode()
+    def sample(self, noise: torch.Tensor, prefix: Prefix, steps: int = 25, step_events=None,
+               graph: bool = False) -> torch.Tensor:
+        """Flow-matching Euler from unit-Gaussian noise [B, 64, H, W] (sampling.py:19-31); ``graph``: every step
+        replays one captured forward (``step_graph``)."""
         sig = sigmas(steps)
         x = noise.float() * sig[0]
         work: dict = {}
         for i in range(steps):
             t = torch.full((x.shape[0],), sig[i], device=x.device)
-            v = self.forward(x.to(torch.bfloat16), t, prefix, work).float()
+            xb = x.to(torch.bfloat16)
+            v = (self.step_graph(xb, t, prefix) if graph else self.forward(xb, t, prefix, work)).float()
             x = x + (sig[i + 1] - sig[i]) * v
             if step_events is not None:
                 step_events[i].record()
