@@ -14,7 +14,8 @@
 //                   fp8) into a 256-column fp32 accumulator. Its waits poll with mbarrier.test_wait: a blocking
 //                   try_wait on the issue path costs ~128 cycles per stage, a quarter of the stage's MMA time.
 //   warps 2..5    : scale writers (NVFP4 modes) -- copy the stage's scales from shared memory into this CTA's TMEM
-//                   with tcgen05.st (one warp per TMEM lane quadrant) and arrive on the leader's `ready` barrier.
+//                   with tcgen05.st (one warp per TMEM lane quadrant) and arrive on the leader's `full` barrier, so
+//                   that one barrier per stage tells the MMA thread both the tiles and the scales are in place.
 //                   tcgen05.cp of the same bytes serialises with the MMAs and costs ~40% of the tensor time;
 //                   tcgen05.st from four warps runs alongside them.
 //   warps 6..13   : epilogue, two warps per TMEM lane quadrant (warp w reads lanes 32*(w%4)..+31, one output row
@@ -427,8 +428,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   // tiles (each CTA's tensor loads complete on it), the follower's is unused
   uint64_t* full = reinterpret_cast<uint64_t*>(sOut + OUT_BYTES);
   uint64_t* empty = full + STAGES;          // the stage's MMAs completed (commit from the group's MMA thread)
-  uint64_t* ready = empty + STAGES;         // leader: every scale warp of the group finished the stage
-  uint64_t* sff = ready + STAGES;           // a pair: this CTA's scale bytes landed (its scale warps wait here)
+  uint64_t* sff = empty + STAGES;           // NVFP4: this CTA's scale bytes landed (its scale warps wait here)
   uint64_t* acc_full = sff + STAGES;
   uint64_t* acc_empty = acc_full + 1;       // leader: every epilogue warp of the group drained the accumulator
   uint64_t* drain = acc_empty + 1;
@@ -441,9 +441,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int grp = blockIdx.x / CG, ngrp = gridDim.x / CG;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full + s, 1);
+      // leader: its producer's arrive (with the tile bytes of the group) + every scale warp of the group
+      mbar_init(full + s, 1 + (FP4 ? 4 * CG : 0));
       mbar_init(empty + s, 1);
-      mbar_init(ready + s, 4 * CG);
       mbar_init(sff + s, 1);
     }
     mbar_init(acc_full, 1);
@@ -477,10 +477,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   pdl_trigger();
   pdl_wait();
   const uint32_t tmem = *tmem_slot;
-  // the leader's copies of `ready` and `acc_empty`, as shared::cluster addresses
-  uint32_t ready_l = smem_u32(ready), acc_empty_l = smem_u32(acc_empty), full_l = smem_u32(full);
+  // the leader's copies of `full` and `acc_empty`, as shared::cluster addresses
+  uint32_t acc_empty_l = smem_u32(acc_empty), full_l = smem_u32(full);
   if (CG == 2 && rank != 0) {
-    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(ready_l) : "r"(ready_l));
     asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(acc_empty_l) : "r"(acc_empty_l));
     asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(full_l) : "r"(full_l));
   }
@@ -518,17 +517,17 @@ __global__ void __launch_bounds__(THREADS, 1)
             sf_bytes = min(4, p.kb_total - ks * 4) * 512;
             sf_tx = sf_bytes * ((ga < p.sfa_groups) + (g0 < p.sfb_groups) + (g1 < p.sfb_groups));
           }
-          // scale copies complete on this CTA's own barrier: `full` (one CTA) or `sff` (a pair)
-          uint64_t* sf_bar = CG == 2 ? sff + stage : full + stage;
+          // scale copies complete on this CTA's `sff` (its scale warps wait there, then arrive on `full`)
+          uint64_t* sf_bar = sff + stage;
+          if (FP4) mbar_expect_tx(sff + stage, sf_tx);
           if (CG == 2) {
             // both CTAs' operand tiles complete on the leader's `full`, which the leader alone arms (tile loads
             // always count their whole box, rows past the tensor's end included)
             if (rank == 0) mbar_expect_tx(full + stage, 2 * (A_BYTES + B_BYTES_CTA));
-            if (FP4) mbar_expect_tx(sff + stage, sf_tx);
             tma_load_2d_pair(sA + stage * A_BYTES, &tmA, full_l + stage * 8, ks * BKB, arow);
             tma_load_2d_pair(sB + stage * B_BYTES_CTA, &tmB, full_l + stage * 8, ks * BKB, rank == 0 ? rb0 : rb1);
           } else {
-            mbar_expect_tx(full + stage, A_BYTES + B_BYTES_CTA + sf_tx);
+            mbar_expect_tx(full + stage, A_BYTES + B_BYTES_CTA);
             tma_load_2d(sA + stage * A_BYTES, &tmA, full + stage, ks * BKB, arow);
             tma_load_2d(sB + stage * B_BYTES_CTA, &tmB, full + stage, ks * BKB, rb0);
             tma_load_2d(sB + stage * B_BYTES_CTA + 128 * BKB, &tmB, full + stage, ks * BKB, rb1);
@@ -554,11 +553,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!ok) {  // let every copy already in flight land before the CTA exits
         for (int s = 0; s < STAGES; ++s)
           if (issued & (1u << s)) {
-            // one CTA: `full` counts all of its copies; a pair: `sff` this CTA's scale copies and the leader's
-            // `full` both CTAs' tiles (the follower cannot wait on the leader's barrier; it pauses instead, below)
+            // `sff`: this CTA's scale copies; `full`: the tiles (of both CTAs in a pair; the follower cannot wait on
+            // the leader's barrier and pauses instead, below). A `full` phase may also miss scale-warp arrivals
+            // after an abort: its wait then runs to the limit.
             for (int b = 0; b < 2; ++b) {
               const uint64_t* bar = b == 0 ? full + s : sff + s;
-              if ((b == 0 && CG == 2 && rank != 0) || (b == 1 && (CG == 1 || !FP4))) continue;
+              if ((b == 0 && CG == 2 && rank != 0) || (b == 1 && !FP4)) continue;
               const uint32_t a = smem_u32(bar);
               const unsigned long long t0 = globaltimer();
               while (!mbar_try(a, (last_ph >> s) & 1) && (long long)(globaltimer() - t0) < kWaitLimitNs) {
@@ -580,7 +580,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // Lean on purpose: the tensor core's MMA queue is ~2 instructions deep, so every cycle the issuing thread
       // spends between stages is at risk of idling it. Descriptors advance arithmetically (start address >> 4).
       const uint64_t dA0 = desc_sw128(sA), dB0 = desc_sw128(sB);
-      const uint32_t full0 = smem_u32(full), rdy0 = smem_u32(ready), empty0 = smem_u32(empty);
+      const uint32_t full0 = smem_u32(full), empty0 = smem_u32(empty);
       const uint32_t dacc = tmem + ACC_COL;
       int stage = 0;
       uint32_t ph = 0, acc_ph = 0;
@@ -592,35 +592,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_fence_after();
         for (int ks = 0; ks < p.num_ks; ++ks) {
-          const uint32_t fbar = full0 + stage * 8, rbar = rdy0 + stage * 8;
-          uint32_t go;
-          if (CG == 2 && FP4) {   // both CTAs' tiles (leader's `full`), both CTAs' scales in TMEM (`ready`)
-            asm volatile(
-                "{\n\t.reg .pred p, q;\n\t"
-                "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %3;\n\t"
-                "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 q, [%2], %3;\n\t"
-                "and.pred p, p, q;\n\t"
-                "selp.u32 %0, 1, 0, p;\n\t}"
-                : "=r"(go)
-                : "r"(fbar), "r"(rbar), "r"(ph)
-                : "memory");
-          } else if (FP4) {
-            asm volatile(
-                "{\n\t.reg .pred p, q;\n\t"
-                "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %3;\n\t"
-                "mbarrier.test_wait.parity.shared::cta.b64 q, [%2], %3;\n\t"
-                "and.pred p, p, q;\n\t"
-                "selp.u32 %0, 1, 0, p;\n\t}"
-                : "=r"(go)
-                : "r"(fbar), "r"(rbar), "r"(ph)
-                : "memory");
-          } else {
-            go = mbar_test(fbar, ph);
-          }
-          if (!go) {
-            const bool waited = mbar_wait_slow<true>(fbar, ph, p.err, 0x202) &&
-                                (!FP4 || mbar_wait_slow<true>(rbar, ph, p.err, 0x203));
-            if (!waited) {
+          // one barrier: the stage's tiles (both CTAs' in a pair) and, NVFP4, every scale warp's TMEM writes
+          const uint32_t fbar = full0 + stage * 8;
+          if (!mbar_test(fbar, ph)) {
+            if (!mbar_wait_slow<true>(fbar, ph, p.err, 0x202)) {
               ok = false;
               break;
             }
@@ -675,7 +650,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int ks = 0; ks < p.num_ks; ++ks) {
         // the stage's scales landed; its TMEM scale buffer is free too: the producer re-armed the stage only after
         // the MMAs of its previous use completed
-        if (!mbar_wait<false>(CG == 2 ? sff + stage : full + stage, ph, p.err, 0x401)) {
+        if (!mbar_wait<false>(sff + stage, ph, p.err, 0x401)) {
           ok = false;
           break;
         }
@@ -706,8 +681,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         __syncwarp();
         if (lane == 0) {
-          if (CG == 2 && rank != 0) mbar_arrive_cluster(ready_l + stage * 8);   // the leader's barrier
-          else mbar_arrive(ready + stage);
+          if (CG == 2 && rank != 0) mbar_arrive_cluster(full_l + stage * 8);   // the leader's barrier
+          else mbar_arrive(full + stage);
         }
         if (++stage == STAGES) {
           stage = 0;
