@@ -318,6 +318,23 @@ def config_legs(dev, fp4_peak: float, fp8_peak: float, hbm_gbs: float) -> dict:
         fl = 2 * M3 * n * k
         res[name] = {"gemm_us": t8, "tflops": fl / t8 / 1e6, "frac_fp8_peak": fl / t8 / 1e6 / fp8_peak}
     out["configs[3]"] = res
+
+    # GGUF block decode (the checkpoint loader's hot loop): one [16384, 3072] weight per quantized type -> bf16
+    rows, cols = 16384, 3072
+    res = {"workload": "GGUF Q8_0 / Q4_K / Q5_K / Q6_K weight [16384, 3072] (uniform random code bytes, block scales "
+                       "fixed finite f16) decoded to bf16; bytes = raw blocks read + bf16 written"}
+    gen = torch.Generator(device=dev).manual_seed(31)
+    for kind, scale_cols in (("Q8_0", (0,)), ("Q4_K", (0, 2)), ("Q5_K", (0, 2)), ("Q6_K", (208,))):
+        vals, nbytes = _lib.gguf_block(kind)
+        raw = torch.randint(0, 256, (rows * cols // vals, nbytes), dtype=torch.uint8, device=dev, generator=gen)
+        for c in scale_cols:
+            raw[:, c], raw[:, c + 1] = 0x1C, 0x1C                 # f16 0x1C1C = 0.00412
+        y = torch.empty(rows * cols, dtype=torch.bfloat16, device=dev)
+        t = timed(lambda: _lib.gguf_dequant(kind, raw, y))
+        nb = raw.numel() + 2 * y.numel()
+        res[kind] = {"us": t, "gbs": nb / t / 1e3, "frac_hbm": nb / t / 1e3 / hbm_gbs, "bytes": nb}
+        del raw, y
+    out["gguf_decode"] = res
     out["peaks"] = {"fp4_tflops": fp4_peak, "fp8_tflops": fp8_peak, "hbm_gbs": hbm_gbs}
     del flush
     _ = np
@@ -406,7 +423,10 @@ def dit_leg(world: int, rank: int, dev, barrier, reduce_max) -> dict:
             "img_per_s": DIT_SEEDS / sample_s, "sample_s": sample_s, "seeds": DIT_SEEDS,
             "seeds_per_rank": counts, "steps": DIT_STEPS, "scaling": "strong (32 seeds split across ranks)",
             "parallelism": f"dp{world} (weight replica per rank, no collective)",
-            "weights_gb": model.nbytes() / 1e9, "launches_per_step": 9 * model.cfg.layers + 1,
+            "weights_gb": model.nbytes() / 1e9, "libtfb_launches_per_step": 7 * model.cfg.layers + 1,
+            "launches_note": "per image block: AdaLN+quant, qkv GEMM, q/k/v RMS-RoPE, out GEMM (+residual), AdaLN+quant, "
+                             "gate/up+SwiGLU GEMM, down GEMM (+residual); plus the final AdaLN. torch adds SDPA per "
+                             "block and the embedders; the prefix rows stay in per-block K/V buffers (no copies)",
             "tensor_parallel_latency": tp_lat, "finite": ok, "clocks": clk.report(),
             "timing": "CUDA events on the launching stream, max over ranks; latency = median of 10 steps after 3 "
                       "warm-up, each step one replayed CUDA graph of the forward (eager launches: step_ms_eager); "

@@ -171,6 +171,20 @@ tfb_status tfb_rms_rope_qkv(const void* src, int64_t B, int64_t N, int64_t H, in
  * Replaces the Triton _swiglu_kernel (tfimage/kernels.py:73-92). F % 8 == 0. */
 tfb_status tfb_swiglu(const void* gu, int64_t M, int64_t F, void* out, void* stream);
 
+/* GGUF quantized block types decoded on the device (ggml type ids) and output element types. */
+enum { TFB_GGUF_Q8_0 = 8, TFB_GGUF_Q4_K = 12, TFB_GGUF_Q5_K = 13, TFB_GGUF_Q6_K = 14 };
+enum { TFB_DT_F32 = 0, TFB_DT_F16 = 1, TFB_DT_BF16 = 2 };
+
+/* Bytes per block of a TFB_GGUF_* type (-1 for any other type); *values_per_block (nullable) receives 32 or 256. */
+int64_t tfb_gguf_block_bytes(int type, int64_t* values_per_block);
+
+/* GGUF block decode: raw = n_values / values_per_block consecutive blocks of `type` (device, 16-byte aligned) ->
+ * out (device, 16-byte aligned) n_values elements of out_dtype, in block order (the tensor's row-major order).
+ * Arithmetic: one fp32 rounding per operation in the reference's order, then round to nearest even to out_dtype.
+ * Replaces the torch decoders _q8_0 / _q6_k / _q4_k / _q5_k and the .to(dtype) of dequantize
+ * (tfimage/gguf_load.py:21-86). n_values % values_per_block == 0. */
+tfb_status tfb_gguf_dequant(int type, const uint8_t* raw, int64_t n_values, void* out, int out_dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

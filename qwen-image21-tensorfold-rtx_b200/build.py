@@ -21,7 +21,7 @@ CSRC = HERE / "csrc"
 INCLUDE = ROOT / "include"
 OUT = HERE / "tfimage" / "libtfb.so"
 OBJ = HERE / "_build"
-SOURCES = ["host.cu", "quant.cu", "fusions.cu", "gemm.cu"]
+SOURCES = ["host.cu", "quant.cu", "fusions.cu", "gemm.cu", "gguf.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr", "-I", str(INCLUDE),
          "-I", str(CSRC)]

@@ -45,10 +45,15 @@ SIGNATURES = {
     "tfb_rms_rope_qkv": [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_float, c_vp, c_i64,
                          c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp],
     "tfb_swiglu": [c_vp, c_i64, c_i64, c_vp, c_vp],
+    "tfb_gguf_block_bytes": [c_int, ctypes.POINTER(c_i64)],
+    "tfb_gguf_dequant": [c_int, c_vp, c_i64, c_vp, c_int, c_vp],
 }
-RESTYPES = {"tfb_version": c_int, "tfb_last_error": ctypes.c_char_p, "tfb_sf_tiled_bytes": c_i64}
+RESTYPES = {"tfb_version": c_int, "tfb_last_error": ctypes.c_char_p, "tfb_sf_tiled_bytes": c_i64,
+            "tfb_gguf_block_bytes": c_i64}
 
 SF_ROWS, SF_TILED = 0, 1
+GGUF_TYPES = {"Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}     # TFB_GGUF_* (ggml type ids)
+OUT_DTYPES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}  # TFB_DT_*
 MLP_STATIC_SCRATCH_BYTES = 32 << 20   # TFB_MLP_STATIC_SCRATCH_BYTES
 STATUS = {0: "OK", 1: "BAD_SHAPE", 2: "BAD_ALIGN", 3: "BAD_ARCH", 4: "DEVICE_TIMEOUT", 5: "CUDA_ERR", 6: "BAD_ARG"}
 
@@ -268,3 +273,24 @@ def swiglu(gu, out) -> None:
     _cuda(gu, out)
     M, F2 = gu.shape
     check(load().tfb_swiglu(gu.data_ptr(), M, F2 // 2, out.data_ptr(), _stream(gu)))
+
+
+def gguf_block(kind: str) -> tuple[int, int]:
+    """(values, bytes) per block of a GGUF type decoded here."""
+    v = c_i64(0)
+    b = load().tfb_gguf_block_bytes(GGUF_TYPES[kind], ctypes.byref(v))
+    return int(v.value), int(b)
+
+
+def gguf_dequant(kind: str, raw, out) -> None:
+    """raw uint8 blocks of ``kind`` -> ``out`` (f32 / f16 / bf16, out.numel() values), on raw's stream."""
+    _cuda(raw, out)
+    if kind not in GGUF_TYPES:
+        raise TfbError(f"GGUF type {kind} is not decoded here (decoded: {', '.join(GGUF_TYPES)})")
+    if out.dtype not in OUT_DTYPES or not out.is_contiguous():
+        raise TfbError("gguf_dequant: out must be a contiguous f32 / f16 / bf16 tensor")
+    vals, nbytes = gguf_block(kind)
+    if raw.numel() * vals != out.numel() * nbytes:
+        raise TfbError(f"gguf_dequant: {raw.numel()} bytes of {kind} do not hold {out.numel()} values")
+    check(load().tfb_gguf_dequant(GGUF_TYPES[kind], raw.data_ptr(), out.numel(), out.data_ptr(),
+                                  OUT_DTYPES[out.dtype], _stream(raw)))

@@ -9,8 +9,9 @@ the model input [B, 64, 64, 64] (4096 tokens); the prompt is a [256, 3584] conte
   t = 0 and attending causally among themselves; every block's keys and values are kept.
 * Step (qwen_image21.py:259-299, _block :204-216): only the image rows run. Per block: AdaLN (+ shift) fused with
   the NVFP4 quantizer of the qkv input, qkv GEMM, RMSNorm + RoPE of q and k (k written behind the kept prefix in
-  one key buffer, v copied beside it), SDPA over [prefix, image], out GEMM, gated residual, AdaLN fused with the
-  quantizer of the MLP input, the fused gate/up SwiGLU -> NVFP4 -> down pair, gated residual.
+  the block's key buffer, v copied beside it), SDPA over [prefix, image], out GEMM, gated residual, AdaLN fused
+  with the quantizer of the MLP input, the fused gate/up SwiGLU -> NVFP4 -> down pair, gated residual. Each block
+  has its own key / value buffers whose prefix rows are written once per prompt, not copied in every step.
 * Sampler: flow-matching Euler on shifted sigmas (sampling.py:12-31).
 
 Linears are ``linear.make(kind, w)`` modules; static input scales come from ``calibrate`` (the reference's
@@ -19,8 +20,9 @@ calibrate.py procedure: a dynamic-scale run, then 4 x the largest input scale se
 
 from __future__ import annotations
 
+import itertools
 import math
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import torch
 import torch.nn.functional as F
@@ -90,11 +92,15 @@ class Block:
     tp: object = None          # tp.TPMLP: this rank's MLP shard (single-image latency mode)
 
 
+_PREFIX_VERSIONS = itertools.count(1)
+
+
 @dataclass
 class Prefix:
     kv: list                   # per block (k, v) [1, P, H, D] bf16
     length: int
     next_pos: int
+    version: int = field(default_factory=lambda: next(_PREFIX_VERSIONS))   # new on every (re)build
 
 
 def _sdpa(q, k, v, causal=False):
@@ -108,6 +114,9 @@ class SynthMMDiT:
 
     def __init__(self, cfg: DitConfig = DitConfig(), kind: str = "nvfp4", device="cuda", seed: int = 0):
         self.cfg, self.kind, self.device = cfg, kind, torch.device(device)
+        # Per-block key / value buffers that keep the prefix rows across steps (``forward``), used while their total
+        # size stays within this many bytes (None: 40 % of the device's memory); larger batches share one buffer.
+        self.kv_budget: int | None = None
         g = torch.Generator(device=self.device).manual_seed(seed)
         D = cfg.dim
 
@@ -225,29 +234,63 @@ class SynthMMDiT:
                 v = torch.empty_like(k)
             x = self._block(b, x, mod, cos, sin, k, v, causal=True)
             kv.append((k, v))
-        return into if into is not None else Prefix(kv, P, P)
+        if into is None:
+            return Prefix(kv, P, P)
+        into.version = next(_PREFIX_VERSIONS)       # step buffers holding the old rows are refilled on next use
+        return into
 
     # ------------------------------------------------------------------------------------------- step
+    def _kv_buffers(self, work: dict, B: int, rows: int) -> None:
+        """The step's key / value buffers [B, P + N, H, D]: one pair per image block when they fit ``kv_budget``
+        (the prefix rows are written once and stay, qwen_image21.py:287-293 copies them in every block of every
+        step), else one shared pair that each block refills."""
+        cfg = self.cfg
+        shape = (B, rows, cfg.heads, cfg.head_dim)
+        per_pair = 2 * math.prod(shape) * 2
+        budget = self.kv_budget
+        if budget is None:
+            budget = int(0.4 * torch.cuda.get_device_properties(self.device).total_memory) \
+                if self.device.type == "cuda" else 0
+        new = lambda: torch.empty(shape, dtype=torch.bfloat16, device=self.device)   # noqa: E731
+        if per_pair * len(self.img_blocks) <= budget:
+            work.update(kv=[(new(), new()) for _ in self.img_blocks], kv_version=None)
+        else:
+            work.update(kv=None, kv_shared=(new(), new()))
+
+    def _fill_prefix(self, work: dict, prefix: Prefix) -> None:
+        """Copy the prefix rows into the per-block buffers once per prefix version."""
+        if work.get("kv") is None or work["kv_version"] == prefix.version:
+            return
+        P = prefix.length
+        for (kb, vb), (pk, pv) in zip(work["kv"], prefix.kv):
+            kb[:, :P].copy_(pk.expand(kb.shape[0], -1, -1, -1))
+            vb[:, :P].copy_(pv.expand(vb.shape[0], -1, -1, -1))
+        work["kv_version"] = prefix.version
+
     @torch.inference_mode()
     def forward(self, x: torch.Tensor, t: torch.Tensor, prefix: Prefix, work: dict | None = None) -> torch.Tensor:
-        """x [B, 64, H, W] bf16, t [B] -> velocity [B, 64, H, W] bf16. ``work`` caches the step's buffers."""
+        """x [B, 64, H, W] bf16, t [B] -> velocity [B, 64, H, W] bf16. ``work`` caches the step's buffers (and,
+        with per-block key / value buffers, the prefix rows between steps)."""
         cfg = self.cfg
         B, C, Hh, Ww = x.shape
         N, P = Hh * Ww, prefix.length
         work = {} if work is None else work
         key = (B, Hh, Ww, P)
         if work.get("key") != key:
-            kbuf = torch.empty((B, P + N, cfg.heads, cfg.head_dim), dtype=torch.bfloat16, device=self.device)
-            work.update(key=key, kbuf=kbuf, vbuf=torch.empty_like(kbuf),
-                        rope=rope_table(image_ids(Hh, Ww, prefix.next_pos, self.device), cfg))
-        kbuf, vbuf = work["kbuf"], work["vbuf"]
+            self._kv_buffers(work, B, P + N)
+            work.update(key=key, rope=rope_table(image_ids(Hh, Ww, prefix.next_pos, self.device), cfg))
+        self._fill_prefix(work, prefix)
         cos, sin = work["rope"]
         temb = self._temb(t)
         mod = self._mod(temb, self.mod_img)
         h = F.linear(x.flatten(2).transpose(1, 2), self.img_in).contiguous()
-        for b, (pk, pv) in zip(self.img_blocks, prefix.kv):
-            kbuf[:, :P].copy_(pk.expand(B, -1, -1, -1))
-            vbuf[:, :P].copy_(pv.expand(B, -1, -1, -1))
+        for i, (b, (pk, pv)) in enumerate(zip(self.img_blocks, prefix.kv)):
+            if work["kv"] is not None:
+                kbuf, vbuf = work["kv"][i]
+            else:
+                kbuf, vbuf = work["kv_shared"]
+                kbuf[:, :P].copy_(pk.expand(B, -1, -1, -1))
+                vbuf[:, :P].copy_(pv.expand(B, -1, -1, -1))
             h = self._block(b, h, mod, cos, sin, kbuf, vbuf)
         h = K.adaln(h, F.linear(F.silu(temb), self.norm_out).unsqueeze(1), cfg.eps)
         out = F.linear(h, self.proj_out)
@@ -263,6 +306,8 @@ class SynthMMDiT:
         graphs = self.__dict__.setdefault("_graphs", {})
         key = (tuple(x.shape), id(prefix))
         entry = graphs.get(key)
+        if entry is not None:
+            self._fill_prefix(entry[4], prefix)               # a rebuilt prefix: new rows, outside the graph
         if entry is None:
             xs, ts, work = x.clone(), t.clone(), {}
             self.forward(xs, ts, prefix, work)                   # warm-up: one-time set-up outside the capture
@@ -272,8 +317,8 @@ class SynthMMDiT:
             with torch.cuda.stream(side), torch.cuda.graph(g, stream=side):
                 out = self.forward(xs, ts, prefix, work)
             torch.cuda.current_stream(x.device).wait_stream(side)
-            entry = graphs[key] = (g, xs, ts, out, work)
-        g, xs, ts, out, _ = entry
+            entry = graphs[key] = (g, xs, ts, out, work, prefix)   # the prefix held: its id stays unique
+        g, xs, ts, out = entry[:4]
         xs.copy_(x)
         ts.copy_(t)
         g.replay()

@@ -11,7 +11,9 @@ What each file pins:
   * ``fusions.npz`` -- ``tfimage.kernels.adaln`` / ``rms_rope`` / ``swiglu`` (kernels.py:14-92), run on CPU by
     Triton's interpreter, plus ``_rope_table`` / ``_image_ids`` (qwen_image21.py:63-72,164-169);
   * ``fp8.npz`` -- ``tfimage.linear.Fp8Linear`` (linear.py:70-102) on CPU: ``w8``, ``ws``, the e4m3 activations
-    it hands to ``torch._scaled_mm`` (captured by wrapping that call) and its bf16 output, dynamic and static act.
+    it hands to ``torch._scaled_mm`` (captured by wrapping that call) and its bf16 output, dynamic and static act;
+  * ``gguf.npz`` -- ``tfimage.gguf_load.dequantize`` (gguf_load.py:17-86) on CPU for Q8_0 / Q4_K / Q5_K / Q6_K
+    blocks made by ``oracle.gguf.random_blocks``: the fp32 values and the bf16 output.
 bf16 tensors are stored as uint16 bit patterns.
 """
 
@@ -46,11 +48,14 @@ def extract_deq(ref: Path):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
+    ap.add_argument("--only", choices=["gguf"], help="regenerate one fixture only")
     args = ap.parse_args()
     ref = Path(args.reference).resolve()
     os.environ["TRITON_INTERPRET"] = "1"
     sys.path.insert(0, str(ref))
     import torch
+    if args.only == "gguf":
+        return make_gguf()
     from tfimage import kernels as K
     from tfimage import linear as L
     from tfimage.qwen_image21 import Config, QwenImage21, _rope_table
@@ -123,7 +128,26 @@ def main():
         fp[f"{tag}_ws"] = lin.ws.reshape(1).numpy()
     fp.update(w=w.numpy(), x=bits(x), static_act=np.float32(0.05))
     np.savez_compressed(HERE / "fp8.npz", **fp)
+    make_gguf()
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
+
+
+def make_gguf():
+    import torch
+    from tfimage import gguf_load
+
+    sys.path.insert(0, str(HERE.parents[1]))
+    from oracle.gguf import TYPES, random_blocks
+
+    out = {}
+    for i, kind in enumerate(TYPES):
+        vals, nbytes, _ = TYPES[kind]
+        raw = random_blocks(kind, 24, 100 + i)
+        shape = (len(raw) // nbytes * vals // 64, 64)
+        out[f"{kind}_raw"] = raw
+        out[f"{kind}_f32"] = gguf_load.dequantize(kind, raw, shape, "cpu", torch.float32).numpy()
+        out[f"{kind}_bf16"] = bits(gguf_load.dequantize(kind, raw, shape, "cpu", torch.bfloat16))
+    np.savez_compressed(HERE / "gguf.npz", **out)
 
 
 if __name__ == "__main__":

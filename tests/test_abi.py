@@ -82,3 +82,22 @@ def test_fp8_weight_conversion_matches_reference_fixture():
 def test_ops_refuse_cpu_tensors():
     with pytest.raises(_lib.TfbError):
         _lib.quant_nvfp4(torch.zeros(4, 64, dtype=torch.bfloat16), 1.0)
+
+
+def test_gguf_block_table_and_host_checks():
+    from oracle import gguf as og
+    from tfimage import gguf_load
+
+    lib = _lib.load()
+    for kind, (vals, nbytes, type_id) in og.TYPES.items():
+        assert _lib.GGUF_TYPES[kind] == type_id
+        assert _lib.gguf_block(kind) == (vals, nbytes)
+    assert lib.tfb_gguf_block_bytes(2, None) == -1                    # Q4_0: not decoded here
+    assert set(gguf_load.DECODERS) == {"Q8_0", "Q6_K", "Q5_K", "Q4_K"}
+    f16 = np.arange(6, dtype=np.float16)
+    y = gguf_load.dequantize("F16", f16, (2, 3), "cpu", torch.float32)  # pass-through types are a cast
+    assert torch.equal(y, torch.arange(6, dtype=torch.float32).view(2, 3))
+    with pytest.raises(ValueError, match="IQ4_XS"):
+        gguf_load.dequantize("IQ4_XS", np.zeros(136, np.uint8), (256,), "cpu")
+    with pytest.raises(_lib.TfbError, match="no CPU path"):
+        gguf_load.dequantize("Q4_K", og.random_blocks("Q4_K", 1, 0), (256,), "cpu")

@@ -213,3 +213,33 @@ def test_graph_step_matches_eager(model, dev):
         assert torch.equal(eager, replay)
     noise = torch.randn((1, 64, 16, 16), generator=g).to(dev)
     assert torch.equal(m.sample(noise, prefix, steps=3), m.sample(noise, prefix, steps=3, graph=True))
+
+
+def test_persistent_prefix_kv_matches_shared_buffer(model, dev):
+    """Per-block key / value buffers (prefix rows written once) give the shared-buffer path's output bit for bit,
+    eager and from a step graph, and pick up a prefix rebuilt in place (new prompt) before the next replay."""
+    m, ctx = model
+    prefix = m.build_prefix(ctx)
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn((2, 64, 16, 16), generator=g).to(torch.bfloat16).to(dev)
+    t = torch.tensor([0.8, 0.4], device=dev)
+    per_block: dict = {}
+    y1 = m.forward(x, t, prefix, per_block)
+    assert per_block["kv"] is not None and len(per_block["kv"]) == m.cfg.layers
+    m.kv_budget = 0
+    try:
+        shared: dict = {}
+        y0 = m.forward(x, t, prefix, shared)
+        assert shared["kv"] is None
+    finally:
+        m.kv_budget = None
+    assert torch.equal(y0, y1)
+    assert torch.equal(m.forward(x, t, prefix, per_block), y1)          # second step: no prefix copies
+    yg = m.step_graph(x, t, prefix).clone()
+    assert torch.equal(yg, y1)
+    ctx2 = torch.randn(ctx.shape, generator=g).to(dev)
+    m.build_prefix(ctx2, into=prefix)                                    # new prompt into the same buffers
+    y2 = m.forward(x, t, prefix, per_block)
+    assert not torch.equal(y2, y1)
+    assert torch.equal(y2, m.forward(x, t, m.build_prefix(ctx2), {}))
+    assert torch.equal(m.step_graph(x, t, prefix), y2)

@@ -7,6 +7,7 @@ import pytest
 import torch
 
 from oracle import fp8, fusions, mlp, nvfp4
+from oracle import gguf as ogguf
 
 GOLD = Path(__file__).resolve().parent / "golden"
 
@@ -197,3 +198,38 @@ def test_mlp_oracle_composition():
     y, parts = mlp.forward(x, guc, gus, ggu, dc, ds, gd, ax, 0.01, return_parts=True)
     assert y.shape == (M, K) and parts["h_codes"].shape == (M, F // 2)
     np.testing.assert_array_equal(parts["h"], fusions.swiglu(parts["gu"]))
+
+
+@pytest.mark.parametrize("kind", list(ogguf.TYPES))
+def test_gguf_decoders_match_reference(kind):
+    """oracle.gguf against the reference's own decoders (gguf_load.py:17-86, run on CPU): fp32 and bf16, bit-exact."""
+    z = np.load(GOLD / "gguf.npz")
+    raw = z[f"{kind}_raw"]
+    y = ogguf.dequantize(kind, raw)
+    assert np.array_equal(y.view(np.uint32), z[f"{kind}_f32"].reshape(-1).view(np.uint32))
+    yb = ogguf.dequantize(kind, raw, "bf16")
+    assert np.array_equal((yb.view(np.uint32) >> 16).astype(np.uint16), z[f"{kind}_bf16"].reshape(-1))
+
+
+@pytest.mark.parametrize("kind", list(ogguf.TYPES))
+def test_gguf_decoders_match_gguf_py(kind):
+    """oracle.gguf against gguf-py 0.19.0's numpy decoders (ggml's block formats), bit-exact in fp32, on blocks
+    with every byte value in the code / scale fields."""
+    quants = pytest.importorskip("gguf.quants")
+    from gguf import GGMLQuantizationType
+
+    vals, nbytes, type_id = ogguf.TYPES[kind]
+    assert int(getattr(GGMLQuantizationType, kind)) == type_id
+    raw = ogguf.random_blocks(kind, 2000, 7)
+    ref = quants.dequantize(raw.reshape(-1, nbytes), getattr(GGMLQuantizationType, kind)).reshape(-1)
+    y = ogguf.dequantize(kind, raw)
+    assert y.size == raw.size // nbytes * vals
+    assert np.array_equal(y.view(np.uint32), ref.astype(np.float32).view(np.uint32))
+
+
+def test_gguf_f16_output_and_bad_length():
+    raw = ogguf.random_blocks("Q4_K", 3, 1)
+    y = ogguf.dequantize("Q4_K", raw)
+    assert np.array_equal(ogguf.dequantize("Q4_K", raw, "f16"), y.astype(np.float16).astype(np.float32))
+    with pytest.raises(ValueError):
+        ogguf.dequantize("Q4_K", raw[:-1])
