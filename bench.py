@@ -390,21 +390,28 @@ def dit_leg(world: int, rank: int, dev, barrier, reduce_max) -> dict:
     # single-image latency with the MLP split over the ranks (NCCL all-reduce of the bf16 down partial per block)
     tp_lat = None
     if world > 1:
-        model.enable_tp()
-        for _ in range(3):
-            model.forward(x1, t1, prefix, work)
-        barrier()
-        lat = [(ev(), ev()) for _ in range(10)]
-        for a, b in lat:
-            a.record(stream)
-            model.forward(x1, t1, prefix, work)
-            b.record(stream)
-        barrier()
-        tp_lat = {"world": world, "step_ms": reduce_max(statistics.median(a.elapsed_time(b) for a, b in lat)),
+        def tp_step_ms(p2p: bool) -> float:
+            model.enable_tp(p2p=p2p)
+            for _ in range(3):
+                model.forward(x1, t1, prefix, work)
+            barrier()
+            lat = [(ev(), ev()) for _ in range(10)]
+            for a, b in lat:
+                a.record(stream)
+                model.forward(x1, t1, prefix, work)
+                b.record(stream)
+            barrier()
+            ms = reduce_max(statistics.median(a.elapsed_time(b) for a, b in lat))
+            model.disable_tp()
+            return ms
+
+        tp_lat = {"world": world, "step_ms": tp_step_ms(True), "step_ms_nccl": tp_step_ms(False),
                   "split": "MLP: gate/up columns (pairs kept local) and down rows over the ranks; attention, qkv, "
                            "out replicated",
-                  "collective": "NCCL all-reduce (sum) of the bf16 down partial [4096, 3072] per block"}
-        model.disable_tp()
+                  "collective": "step_ms: the reduction fused into the down GEMM (tfb_gemm_nvfp4_tp: partial tiles "
+                                "sent to their row owner with NVLink peer stores while the GEMM runs, reduced with "
+                                "the gated residual in the owner's epilogue, x rows stored into every rank); "
+                                "step_ms_nccl: NCCL all-reduce (sum) of the bf16 down partial [4096, 3072] per block"}
 
     # throughput: this rank's seeds through the whole sampler, the prompt's prefix built inside the timed region
     model.sample(noise, prefix, 1, graph=True)           # captures this batch's step graph (one-time)

@@ -171,6 +171,46 @@ tfb_status tfb_rms_rope_qkv(const void* src, int64_t B, int64_t N, int64_t H, in
  * Replaces the Triton _swiglu_kernel (tfimage/kernels.py:73-92). F % 8 == 0. */
 tfb_status tfb_swiglu(const void* gu, int64_t M, int64_t F, void* out, void* stream);
 
+/* ---- Tensor-parallel MLP down projection with the cross-GPU reduction fused into the GEMM (no counterpart in the
+ * reference, which runs on one GPU; it replaces the NCCL all-reduce + addcmul_ of the K-split down projection of
+ * tfimage/tp.py, the reference's linear.py:136-150 MLP split over ranks). One process per GPU, all on one node. */
+#define TFB_TP_MAX_WORLD 8
+
+/* Every rank's communication buffer as mapped in this process (base[rank] = its own; the others through
+ * tfb_ipc_open), and the shape it was laid out for. */
+typedef struct {
+  int world, rank;
+  void* base[TFB_TP_MAX_WORLD];
+  int64_t max_rows, n_cols;
+} tfb_tp_comm;
+
+/* Bytes of one rank's communication buffer for `world` ranks and up to max_rows x n_cols bf16 rows, and (nullable)
+ * offsets[4] of its regions: x (the replicated residual stream [max_rows, n_cols] bf16, row stride n_cols), the
+ * receive slots, the partial counters, the x counters. The buffer must be zero before its first use, on every rank
+ * before any rank's first call; it serves one (M, N) shape until it is zeroed again. -1 on bad arguments. */
+int64_t tfb_tp_layout(int world, int64_t max_rows, int64_t n_cols, int64_t* offsets);
+
+/* x += gate * (sum over ranks of bf16(alpha * a_r @ b_r^T)), x = the comm's x region [M, N] on every rank: this
+ * rank's K-slice (a_codes [M, K/2], b_codes [N, K/2], tiled scales) is multiplied on tcgen05; the M rows are cut into
+ * one chunk per rank; tiles of other ranks' chunks are sent to their owners over NVLink as they finish, tiles of
+ * this rank's chunk add the received partials (bf16 sum in rank order, fp32) and the gated residual
+ * (bf16(fma(y, gate, x)), the arithmetic of tfb_gemm_nvfp4_resid) and are stored into every rank's x. Every rank
+ * calls it with the same M, N, K, gate and epoch (1, 2, 3, ... per call on this buffer). x rows of other ranks'
+ * chunks are complete only after tfb_tp_wait. Waits are bounded (TFB_DEVICE_TIMEOUT via tfb_device_status). */
+tfb_status tfb_gemm_nvfp4_tp(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* b_codes, const uint8_t* b_sf,
+                             int64_t M, int64_t N, int64_t K, float alpha, const void* gate, int64_t ld_gate,
+                             int64_t rows_per_gate, const tfb_tp_comm* comm, uint32_t epoch, void* stream);
+
+/* Enqueues a wait (bounded) until every other rank's x rows of call `epoch` are in this rank's x. */
+tfb_status tfb_tp_wait(const tfb_tp_comm* comm, int64_t M, int64_t N, uint32_t epoch, void* stream);
+
+/* CUDA IPC between the processes of one node: the 64-byte handle of the device allocation holding `ptr`, and ptr's
+ * offset inside it; tfb_ipc_open maps another process's allocation here (*ptr = its base + offset); tfb_ipc_close
+ * unmaps it (ptr as returned by tfb_ipc_open, with the same offset). */
+tfb_status tfb_ipc_handle(const void* ptr, uint8_t* handle, int64_t* offset);
+tfb_status tfb_ipc_open(const uint8_t* handle, int64_t offset, void** ptr);
+tfb_status tfb_ipc_close(void* ptr, int64_t offset);
+
 /* GGUF quantized block types decoded on the device (ggml type ids) and output element types. */
 enum { TFB_GGUF_Q8_0 = 8, TFB_GGUF_Q4_K = 12, TFB_GGUF_Q5_K = 13, TFB_GGUF_Q6_K = 14 };
 enum { TFB_DT_F32 = 0, TFB_DT_F16 = 1, TFB_DT_BF16 = 2 };

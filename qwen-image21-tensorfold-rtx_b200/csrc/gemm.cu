@@ -44,6 +44,11 @@ constexpr int SFB_BYTES = 2 * 4 * 512;        // two 128-row groups
 constexpr int OUT_WARP_BYTES = 32 * 128;      // epilogue staging per warp: 32 rows x 128 B (one TMA store box)
 constexpr int OUT_BYTES = 8 * OUT_WARP_BYTES; // 8 epilogue warps
 constexpr int THREADS = 448;
+// MODE_FP4_TP adds warp 14: it turns the epilogue's finished tiles into cross-GPU signals (a system-scope fence
+// and a counter add on the peer per tile), so the epilogue warps never stall on a fence; kSigSlots tiles in flight.
+constexpr int SIG_WARP = 14, kSigSlots = 4;
+template <int MODE>
+constexpr int kThreads = MODE == 4 ? THREADS + 32 : THREADS;
 constexpr int EPI_WARP0 = 6, SF_WARP0 = 2;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t ACC_COL = 0;               // accumulator: columns [0, 256)
@@ -52,7 +57,14 @@ constexpr uint32_t SF_STAGE_COLS = 48;
 
 // MODE_FP4_RESID: NVFP4 GEMM whose epilogue adds the gated result into a bf16 residual stream in place,
 // y = bf16(fma(bf16(alpha * acc), gate[row / rows_per_gate, col], y)) -- torch's x.addcmul_(linear(a), gate).
-enum Mode { MODE_FP4 = 0, MODE_FP8 = 1, MODE_FP4_SWIGLU = 2, MODE_FP4_RESID = 3 };
+// MODE_FP4_TP: the K-split (tensor-parallel) down projection with the cross-GPU reduction fused into the
+// epilogue. The M rows are cut into one chunk per rank; rank r computes its bf16 partial of every tile, sends
+// the tiles of other ranks' chunks to their owners over NVLink (peer stores into the owner's receive slot, then a
+// per-tile counter on the owner), and for the tiles of its own chunk adds the received partials,
+// x = bf16(fma(bf16(sum over ranks of the partials), gate, x)), and stores the new x rows locally and into every
+// other rank's x (again with a per-tile counter). Tiles of other ranks' chunks go first, so by the time a rank
+// reaches its own chunk the partials for it have been sent a wave of tiles earlier.
+enum Mode { MODE_FP4 = 0, MODE_FP8 = 1, MODE_FP4_SWIGLU = 2, MODE_FP4_RESID = 3, MODE_FP4_TP = 4 };
 
 struct Params {
   int M, N;              // output rows / cols (swiglu: N = F, the hidden width)
@@ -80,6 +92,14 @@ struct Params {
   int64_t ld_gate;
   int64_t rows_per_gate;
   int* err;
+  // MODE_FP4_TP
+  int tp_world, tp_rank;
+  int tp_chunk_mb;       // M blocks (BM * CG rows) per rank's chunk
+  int tp_chunk_rows;
+  int tp_tiles_chunk;    // flag slots per (sender or owner, chunk): tp_chunk_mb * num_n
+  uint32_t tp_target;    // a tile's counter value once both CTAs of its group signalled this launch: CG * epoch
+  uint8_t* tp_base[TFB_TP_MAX_WORLD];   // every rank's communication buffer as mapped here (this rank's included)
+  int64_t tp_r_off, tp_fp_off, tp_fx_off;
 };
 
 // ----------------------------------------------------------------------------------------------- PTX wrappers
@@ -396,6 +416,53 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   nb = idx / gm;
 }
 
+// MODE_FP4_TP: the chunks in the order rank+1, rank+2, ..., rank (this rank's own chunk last), each in the banded
+// order above over its own M blocks. Every role of the kernel maps tiles through here.
+template <int MODE>
+__device__ __forceinline__ void map_tile(const Params& p, int tile, int& mb, int& nb) {
+  if constexpr (MODE == MODE_FP4_TP) {
+    int li = tile;
+    for (int i = 1; i <= p.tp_world; ++i) {
+      const int c = (p.tp_rank + i) % p.tp_world;
+      const int mbc = max(0, min(p.tp_chunk_mb, p.num_m - c * p.tp_chunk_mb));
+      if (li < mbc * p.num_n) {
+        tile_coords(li, mbc, p.num_n, mb, nb);
+        mb += c * p.tp_chunk_mb;
+        return;
+      }
+      li -= mbc * p.num_n;
+    }
+    mb = nb = 0;   // not reached for tile < num_tiles
+  } else {
+    tile_coords(tile, p.num_m, p.num_n, mb, nb);
+  }
+}
+
+// Cross-GPU counters (MODE_FP4_TP): system-scope acquire / release on a 32-bit counter in this GPU's or a peer's
+// memory, and a bounded wait for a counter to reach `target` (modulo 2^32).
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* a) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(uint32_t* a, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __noinline__ bool wait_counter(const uint32_t* a, uint32_t target, int* err, int code) {
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if ((int32_t)(ld_acquire_sys(a) - target) >= 0) return true;
+    if ((it & 63) == 0) {
+      if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+      if ((long long)(globaltimer() - t0) > kWaitLimitNs) {
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+    __nanosleep(100);
+  }
+}
+
 // --------------------------------------------------------------------------------------------------- the kernel
 // Pipeline depth per (mode, CTA group): an NVFP4 stage holds A 16 KB + B 16 KB per CTA of the group's B half
 // (1 CTA: the whole 32 KB B tile) + 6 KB of scales; FP8 stages have no scales. All fit beside the 32 KB epilogue
@@ -410,7 +477,7 @@ struct Cfg {
 };
 
 template <int MODE, int CG>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(kThreads<MODE>, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmY, const Params p) {
   using C = Cfg<MODE, CG>;
@@ -433,7 +500,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* acc_empty = acc_full + 1;       // leader: every epilogue warp of the group drained the accumulator
   uint64_t* drain = acc_empty + 1;
   uint64_t* xbar = drain + 1;               // resid: per epilogue warp, its residual box landed in its staging
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 8);
+  uint64_t* sigbar = xbar + 8;              // TP: every epilogue warp finished the tile's stores (ring of slots)
+  uint64_t* ackbar = sigbar + kSigSlots;    // TP: the signal warp has signalled that slot's tile
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ackbar + kSigSlots);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint32_t rank = 0;                        // CTA rank inside the MMA group (0 = leader, issues the MMAs)
@@ -450,6 +519,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(acc_empty, 8 * CG);
     mbar_init(drain, 1);
     for (int w = 0; w < 8; ++w) mbar_init(xbar + w, 1);
+    for (int k = 0; k < kSigSlots; ++k) {
+      mbar_init(sigbar + k, 8);
+      mbar_init(ackbar + k, 1);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -496,7 +569,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = true;
       for (int tile = grp; ok && tile < p.num_tiles; tile += ngrp) {
         int mb, nb;
-        tile_coords(tile, p.num_m, p.num_n, mb, nb);
+        map_tile<MODE>(p, tile, mb, nb);
         const int arow = mb * (BM * CG) + (int)rank * BM;             // this CTA's A rows
         int rb0, rb1;                                                  // the tile's two 128-row B groups
         if (MODE == MODE_FP4_SWIGLU) {
@@ -690,6 +763,33 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
+  } else if (MODE == MODE_FP4_TP && warp == SIG_WARP) {
+    // ------------------------------------------------------------------------------------------ signal (TP)
+    // Per tile of this CTA, in the epilogue's order: wait until its 8 warps have issued every peer store of the
+    // tile (their CTA-scope arrive orders those stores before this thread's system-scope release, which is
+    // cumulative), then add 1 to the tile's counter on the receiving rank(s): the owner's partial counter for a
+    // tile of another rank's chunk, every other rank's x counter for a tile of this rank's chunk.
+    if (lane == 0) {
+      int seq = 0;
+      for (int tile = grp; tile < p.num_tiles; tile += ngrp, ++seq) {
+        int mb, nb;
+        map_tile<MODE>(p, tile, mb, nb);
+        const int owner = mb / p.tp_chunk_mb;
+        const int tc = (mb - owner * p.tp_chunk_mb) * p.num_n + nb;
+        if (!mbar_wait<false>(sigbar + seq % kSigSlots, (seq / kSigSlots) & 1, p.err, 0x305)) break;
+        __threadfence_system();
+        if (owner != p.tp_rank) {
+          const int slot = (p.tp_rank - owner - 1 + p.tp_world) % p.tp_world;
+          red_release_sys_add(reinterpret_cast<uint32_t*>(p.tp_base[owner] + p.tp_fp_off) +
+                                  (int64_t)slot * p.tp_tiles_chunk + tc, 1u);
+        } else {
+          for (int qr = 1; qr < p.tp_world; ++qr)
+            red_release_sys_add(reinterpret_cast<uint32_t*>(p.tp_base[(p.tp_rank + qr) % p.tp_world] + p.tp_fx_off) +
+                                    (int64_t)p.tp_rank * p.tp_tiles_chunk + tc, 1u);
+        }
+        mbar_arrive(ackbar + seq % kSigSlots);
+      }
+    }
   } else {
     // ------------------------------------------------------------------------------------------ epilogue
     const int q = warp & 3;
@@ -700,13 +800,27 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t acc_ph = 0;
     uint64_t* xb = xbar + (warp - EPI_WARP0);
     uint32_t x_ph = 0, x_pending = 0;             // resid: parity of the next load; a load not yet waited for
+    constexpr bool kResidMode = MODE == MODE_FP4_RESID || MODE == MODE_FP4_TP;
+    int sig_seq = 0;                              // TP: tiles handed to the signal warp so far
+    auto sig_hand_off = [&]() {
+      // slot reuse: the signal warp has finished the tile kSigSlots back
+      if (sig_seq >= kSigSlots && lane == 0)
+        mbar_wait<false>(ackbar + sig_seq % kSigSlots, (sig_seq / kSigSlots - 1) & 1, p.err, 0x306);
+      __syncwarp();                               // every lane's peer stores before lane 0's arrive
+      if (lane == 0) mbar_arrive(sigbar + sig_seq % kSigSlots);
+      ++sig_seq;
+    };
     for (int tile = grp; tile < p.num_tiles; tile += ngrp) {
       int mb, nb;
-      tile_coords(tile, p.num_m, p.num_n, mb, nb);
+      map_tile<MODE>(p, tile, mb, nb);
       const int row0 = mb * (BM * CG) + (int)rank * BM;            // this CTA's first output row
       const int64_t m = (int64_t)row0 + r;
       const bool rows_live = row0 + q * 32 < p.M;
-      if (MODE == MODE_FP4_RESID && lane == 0 && rows_live && nb * BN + half * 128 < p.N) {
+      // MODE_FP4_TP: the rank owning the tile's rows (its chunk) and the tile's index inside that chunk
+      const int owner = MODE == MODE_FP4_TP ? mb / p.tp_chunk_mb : 0;
+      const int tc = MODE == MODE_FP4_TP ? (mb - owner * p.tp_chunk_mb) * p.num_n + nb : 0;
+      const bool resid_tile = MODE == MODE_FP4_RESID || (MODE == MODE_FP4_TP && owner == p.tp_rank);
+      if (kResidMode && resid_tile && lane == 0 && rows_live && nb * BN + half * 128 < p.N) {
         // the first residual box does not depend on the accumulator: fetch it while the tile's MMAs run (the
         // staging box is free once the previous tile's last store has read it)
         tma_store_wait_read();
@@ -822,13 +936,101 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (CG == 2 && rank != 0) mbar_arrive_cluster(acc_empty_l);
           else mbar_arrive(acc_empty);
         }
+        if constexpr (MODE == MODE_FP4_TP) {
+          if (owner != p.tp_rank) {
+            // another rank's rows: this rank's bf16 partial goes to the owner's receive slot for this sender,
+            // through the staging box (swizzled like the TMA boxes) and coalesced 16-byte peer stores
+            const int slot = (p.tp_rank - owner - 1 + p.tp_world) % p.tp_world;
+            uint8_t* dst = p.tp_base[owner] + p.tp_r_off;
+            const int64_t lrow = (int64_t)slot * p.tp_chunk_rows + (row0 + q * 32 - owner * p.tp_chunk_rows);
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              const int col0 = n_base + c * 64;
+              if (lane == 0) tma_store_wait_read();
+              __syncwarp();
+#pragma unroll
+              for (int ch = 0; ch < 8; ++ch)
+                *reinterpret_cast<uint4*>(stg + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
+                    make_uint4(pk[c * 32 + 4 * ch], pk[c * 32 + 4 * ch + 1], pk[c * 32 + 4 * ch + 2],
+                               pk[c * 32 + 4 * ch + 3]);
+              __syncwarp();
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {          // 4 rows x 128 bytes per pass
+                const int rr = i * 4 + (lane >> 3), ck = lane & 7;
+                if (row0 + q * 32 + rr < p.M && col0 + ck * 8 < p.N)
+                  *reinterpret_cast<uint4*>(dst + ((lrow + rr) * p.N + col0 + ck * 8) * 2) =
+                      *reinterpret_cast<const uint4*>(stg + rr * 128 + ((ck ^ (rr & 7)) << 4));
+              }
+              // these generic reads of the box come before any later async-proxy write to it (a TMA load)
+              asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+              __syncwarp();
+            }
+            sig_hand_off();                        // the signal warp tells the owner
+            acc_ph ^= 1;
+            continue;
+          }
+          // this rank's rows: every other rank's partial of the tile has arrived in this rank's receive slots
+          if (lane == 0)
+            for (int s = 0; s + 1 < p.tp_world; ++s)
+              wait_counter(reinterpret_cast<const uint32_t*>(p.tp_base[p.tp_rank] + p.tp_fp_off) +
+                               (int64_t)s * p.tp_tiles_chunk + tc, p.tp_target, p.err, 0x303);
+          __syncwarp();
+        }
         // two 64-column boxes through the 128-byte-swizzled staging buffer and TMA stores (coalesced, async,
         // clipped at the M / N edges); the buffer is reused once the previous store has read it
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const bool live = n_base + c * 64 < p.N && rows_live;
-          if (MODE == MODE_FP4_RESID) {
+          if (kResidMode) {
             if (!live) continue;
+            if constexpr (MODE == MODE_FP4_TP) {
+              // y = bf16(sum of every rank's bf16 partial of this row, in rank order, in fp32), into pk; the loads
+              // of the whole box are independent of each other and of any store, so they are all in flight at once
+              const int64_t lr0 = m - (int64_t)p.tp_rank * p.tp_chunk_rows;   // row inside this rank's chunk
+              const uint8_t* rv = p.tp_base[p.tp_rank] + p.tp_r_off + (lr0 * p.N + n_base + c * 64) * 2;
+              const int64_t slot_bytes = (int64_t)p.tp_chunk_rows * p.N * 2;
+              if (p.tp_world == 2) {
+                uint4 v[8];
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch)
+                  v[ch] = m < p.M && n_base + c * 64 + ch * 8 < p.N
+                              ? __ldcg(reinterpret_cast<const uint4*>(rv) + ch) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {
+                  const uint32_t pv[4] = {v[ch].x, v[ch].y, v[ch].z, v[ch].w};
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    uint32_t& own = pk[c * 32 + 4 * ch + j];
+                    const float o_lo = __uint_as_float(own << 16), o_hi = __uint_as_float(own & 0xFFFF0000u);
+                    const float r_lo = __uint_as_float(pv[j] << 16), r_hi = __uint_as_float(pv[j] & 0xFFFF0000u);
+                    own = p.tp_rank == 0 ? pack_bf16x2(o_lo + r_lo, o_hi + r_hi) : pack_bf16x2(r_lo + o_lo, r_hi + o_hi);
+                  }
+                }
+              } else {
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {
+                  float lo[4] = {0.f, 0.f, 0.f, 0.f}, hi[4] = {0.f, 0.f, 0.f, 0.f};
+                  for (int qr = 0; qr < p.tp_world; ++qr) {
+                    uint4 v = make_uint4(pk[c * 32 + 4 * ch], pk[c * 32 + 4 * ch + 1], pk[c * 32 + 4 * ch + 2],
+                                         pk[c * 32 + 4 * ch + 3]);
+                    if (qr != p.tp_rank) {
+                      const int sl = (qr - p.tp_rank - 1 + p.tp_world) % p.tp_world;
+                      v = m < p.M && n_base + c * 64 + ch * 8 < p.N
+                              ? __ldcg(reinterpret_cast<const uint4*>(rv + sl * slot_bytes) + ch)
+                              : make_uint4(0, 0, 0, 0);
+                    }
+                    const uint32_t vs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                      lo[j] += __uint_as_float(vs[j] << 16);
+                      hi[j] += __uint_as_float(vs[j] & 0xFFFF0000u);
+                    }
+                  }
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) pk[c * 32 + 4 * ch + j] = pack_bf16x2(lo[j], hi[j]);
+                }
+              }
+            }
             if (c == 1 && lane == 0) {               // second box: after the first one's store has read the box
               tma_store_wait_read();
               mbar_expect_tx(xb, OUT_WARP_BYTES);
@@ -847,9 +1049,11 @@ __global__ void __launch_bounds__(THREADS, 1)
               const uint4 xv = *px, gv = __ldg(gp + ch);
               const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, gs[4] = {gv.x, gv.y, gv.z, gv.w};
               uint32_t o[4];
+              uint32_t y2[4] = {pk[c * 32 + 4 * ch], pk[c * 32 + 4 * ch + 1], pk[c * 32 + 4 * ch + 2],
+                                pk[c * 32 + 4 * ch + 3]};
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
-                const uint32_t a2 = pk[c * 32 + 4 * ch + j];
+                const uint32_t a2 = y2[j];
                 const float lo = fmaf(__uint_as_float(a2 << 16), __uint_as_float(gs[j] << 16),
                                       __uint_as_float(xs[j] << 16));
                 const float hi = fmaf(__uint_as_float(a2 & 0xFFFF0000u), __uint_as_float(gs[j] & 0xFFFF0000u),
@@ -870,11 +1074,29 @@ __global__ void __launch_bounds__(THREADS, 1)
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
           if (lane == 0 && live) tma_store_2d(&tmY, stg, n_base + c * 64, row0 + q * 32);
+          if constexpr (MODE == MODE_FP4_TP) {
+            // the new x rows also go to every other rank's copy of x (coalesced 16-byte peer stores from the box;
+            // the TMA store above only reads it too)
+            const int col0 = n_base + c * 64;
+            for (int qr = 1; qr < p.tp_world; ++qr) {
+              uint8_t* dst = p.tp_base[(p.tp_rank + qr) % p.tp_world];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int rr = i * 4 + (lane >> 3), ck = lane & 7;
+                if (row0 + q * 32 + rr < p.M && col0 + ck * 8 < p.N)
+                  *reinterpret_cast<uint4*>(dst + ((int64_t)(row0 + q * 32 + rr) * p.N + col0 + ck * 8) * 2) =
+                      *reinterpret_cast<const uint4*>(stg + rr * 128 + ((ck ^ (rr & 7)) << 4));
+              }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+          }
         }
+        if constexpr (MODE == MODE_FP4_TP) sig_hand_off();   // own tile: the signal warp tells every other rank
       }
       acc_ph ^= 1;
     }
-    if (MODE == MODE_FP4_RESID && x_pending) {     // left the loop with a residual box still in flight
+    if (kResidMode && x_pending) {     // left the loop with a residual box still in flight
       const uint32_t a = smem_u32(xb);
       const unsigned long long t0 = globaltimer();
       while (!mbar_try(a, x_ph) && (long long)(globaltimer() - t0) < kWaitLimitNs) {
@@ -907,7 +1129,7 @@ tfb_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   tfb_status st = device_info(&di);
   if (st != TFB_OK) return st;
   cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(THREADS);
+  cfg.blockDim = dim3(kThreads<MODE>);
   cfg.dynamicSmemBytes = Cfg<MODE, CG>::SMEM;
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
@@ -1045,6 +1267,128 @@ tfb_status gemm_nvfp4_resid(const uint8_t* a, const uint8_t* a_sf, const uint8_t
   return dispatch<MODE_FP4_RESID>(ta, tb, ty, p, M, BN, N, s);
 }
 
+// ------------------------------------------------------------------- tensor-parallel down projection (MODE_FP4_TP)
+namespace {
+
+int64_t tp_round256(int64_t v) { return (v + 255) / 256 * 256; }
+
+// Rows of each rank's chunk: M / world rounded up to whole 256-row pair tiles, so no tile straddles two owners.
+int64_t tp_chunk_rows(int world, int64_t rows) { return ((rows + world - 1) / world + 255) / 256 * 256; }
+
+struct TpLayout {
+  int64_t chunk_rows, tiles_chunk, x, recv, fp, fx, bytes;
+};
+
+// One rank's communication buffer: x [max_rows, n_cols] bf16 (the replicated residual stream), world-1 receive
+// slots [chunk_rows, n_cols] bf16, then the per-tile counters: partials received [world-1][tiles_chunk] and x rows
+// received [world][tiles_chunk] (u32). Counter slots per chunk cover the 128-row single-CTA tiling too.
+TpLayout tp_layout(int world, int64_t max_rows, int64_t n_cols) {
+  TpLayout L{};
+  L.chunk_rows = tp_chunk_rows(world, max_rows);
+  L.tiles_chunk = (L.chunk_rows / BM) * ((n_cols + BN - 1) / BN);
+  L.x = 0;   // the kernel addresses every rank's x at its buffer's base
+  L.recv = tp_round256(max_rows * n_cols * 2);
+  L.fp = L.recv + tp_round256((int64_t)(world - 1) * L.chunk_rows * n_cols * 2);
+  L.fx = L.fp + tp_round256((int64_t)(world - 1) * L.tiles_chunk * 4);
+  L.bytes = L.fx + tp_round256((int64_t)world * L.tiles_chunk * 4);
+  return L;
+}
+
+tfb_status tp_check(const tfb_tp_comm* c, int64_t M, int64_t N, uint32_t epoch, const char* who) {
+  if (!c || c->world < 2 || c->world > TFB_TP_MAX_WORLD || c->rank < 0 || c->rank >= c->world)
+    return fail(TFB_BAD_ARG, "%s: communicator needs 2 <= world <= %d and 0 <= rank < world", who, TFB_TP_MAX_WORLD);
+  for (int q = 0; q < c->world; ++q)
+    if (!c->base[q] || !aligned(c->base[q], 256))
+      return fail(TFB_BAD_ARG, "%s: rank %d's buffer is missing or not 256-byte aligned", who, q);
+  if (M <= 0 || M > c->max_rows || N != c->n_cols)
+    return fail(TFB_BAD_SHAPE, "%s: M=%lld N=%lld outside the buffer's %lld x %lld", who, (long long)M, (long long)N,
+                (long long)c->max_rows, (long long)c->n_cols);
+  if (epoch == 0 || epoch >= (1u << 27)) return fail(TFB_BAD_ARG, "%s: epoch must be in [1, 2^27)", who);
+  return TFB_OK;
+}
+
+// Waits (bounded) until every tile of every other rank's chunk has its x rows in this rank's x.
+__global__ void __launch_bounds__(256) tp_wait_kernel(const uint32_t* fx, int world, int rank, int chunk_mb,
+                                                      int num_m, int num_n, int tiles_chunk, uint32_t target,
+                                                      int* err) {
+  pdl_trigger();
+  pdl_wait();
+  for (int c = 0; c < world; ++c) {
+    if (c == rank) continue;
+    const int mbc = max(0, min(chunk_mb, num_m - c * chunk_mb));
+    for (int t = threadIdx.x; t < mbc * num_n; t += blockDim.x)
+      if (!wait_counter(fx + (int64_t)c * tiles_chunk + t, target, err, 0x304)) return;
+  }
+}
+
+}  // namespace
+
+tfb_status gemm_nvfp4_tp(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf, int64_t M,
+                         int64_t N, int64_t K, float alpha, const void* gate, int64_t ld_gate, int64_t rows_per_gate,
+                         const tfb_tp_comm* comm, uint32_t epoch, cudaStream_t s) {
+  tfb_status st = check_common(M, N, K, "gemm_nvfp4_tp");
+  if (st != TFB_OK) return st;
+  if ((st = tp_check(comm, M, N, epoch, "gemm_nvfp4_tp")) != TFB_OK) return st;
+  if (N % 8 || !aligned(a_sf, 16) || !aligned(b_sf, 16))
+    return fail(TFB_BAD_ALIGN, "gemm_nvfp4_tp: N %% 8 == 0 and 16-byte aligned scales needed");
+  if (!gate || !aligned(gate, 16) || ld_gate < N || ld_gate % 8 || rows_per_gate < 1)
+    return fail(TFB_BAD_ARG, "gemm_nvfp4_tp: gate must be 16-byte aligned bf16 rows (ld_gate >= N, %% 8 == 0) "
+                "and rows_per_gate >= 1");
+  const DeviceInfo* di;
+  if ((st = device_info(&di)) != TFB_OK) return st;
+  const TpLayout L = tp_layout(comm->world, comm->max_rows, comm->n_cols);
+  uint8_t* x = static_cast<uint8_t*>(comm->base[comm->rank]) + L.x;
+  CUtensorMap ta, tb, ty;
+  if ((st = make_tmap_u8(&ta, a, K / 2, M, K / 2, BKB, BM)) != TFB_OK) return st;
+  if ((st = make_tmap_u8(&tb, b, K / 2, N, K / 2, BKB, 128)) != TFB_OK) return st;
+  if ((st = make_tmap_2d(&ty, x, 2, N, M, N * 2, 64, 32, true)) != TFB_OK) return st;
+  Params p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.num_ks = (int)(K / 256 + (K % 256 ? 1 : 0));
+  p.kb_total = (int)(K / 64);
+  p.b_rows = (int)N;
+  p.sfa = a_sf;
+  p.sfb = b_sf;
+  p.sf_chunks = (int)(K / 64);
+  p.sfb_groups = (int)((N + 127) / 128);
+  p.y = x;
+  p.ldy = N;
+  p.alpha = alpha;
+  p.gate = static_cast<const __nv_bfloat16*>(gate);
+  p.ld_gate = ld_gate;
+  p.rows_per_gate = rows_per_gate;
+  p.err = di->err_word;
+  const int cg = cta_group(M);
+  p.tp_world = comm->world;
+  p.tp_rank = comm->rank;
+  p.tp_chunk_rows = (int)tp_chunk_rows(comm->world, M);
+  p.tp_chunk_mb = p.tp_chunk_rows / (BM * cg);
+  p.tp_tiles_chunk = (int)L.tiles_chunk;
+  p.tp_target = (uint32_t)cg * epoch;   // one add per CTA of the tile's group
+  for (int q = 0; q < comm->world; ++q) p.tp_base[q] = static_cast<uint8_t*>(comm->base[q]);
+  p.tp_r_off = L.recv;
+  p.tp_fp_off = L.fp;
+  p.tp_fx_off = L.fx;
+  return dispatch<MODE_FP4_TP>(ta, tb, ty, p, M, BN, N, s);
+}
+
+tfb_status tp_wait(const tfb_tp_comm* comm, int64_t M, int64_t N, uint32_t epoch, cudaStream_t s) {
+  tfb_status st = tp_check(comm, M, N, epoch, "tp_wait");
+  if (st != TFB_OK) return st;
+  const DeviceInfo* di;
+  if ((st = device_info(&di)) != TFB_OK) return st;
+  const TpLayout L = tp_layout(comm->world, comm->max_rows, comm->n_cols);
+  const int cg = cta_group(M);
+  const int chunk_mb = (int)(tp_chunk_rows(comm->world, M) / (BM * cg));
+  const int num_m = (int)((M + BM * cg - 1) / (BM * cg)), num_n = (int)((N + BN - 1) / BN);
+  const uint32_t* fx = reinterpret_cast<const uint32_t*>(static_cast<uint8_t*>(comm->base[comm->rank]) + L.fx);
+  TFB_LAUNCH(tp_wait_kernel, 1, 256, s, fx, comm->world, comm->rank, chunk_mb, num_m, num_n, (int)L.tiles_chunk,
+             (uint32_t)cg * epoch, di->err_word);
+  TFB_CUDA(cudaGetLastError());
+  return TFB_OK;
+}
+
 tfb_status gemm_nvfp4_swiglu(const uint8_t* a, const uint8_t* a_sf, const uint8_t* gu, const uint8_t* gu_sf, int64_t M,
                              int64_t F, int64_t K, float alpha, float h_g, uint8_t* h_codes, uint8_t* h_sf,
                              void* gu_out, void* h_out, cudaStream_t s) {
@@ -1126,6 +1470,29 @@ tfb_status tfb_gemm_nvfp4_resid(const uint8_t* a_codes, const uint8_t* a_sf, con
                                 int64_t ldx, const void* gate, int64_t ld_gate, int64_t rows_per_gate, void* stream) {
   return tfb::gemm_nvfp4_resid(a_codes, a_sf, b_codes, b_sf, M, N, K, alpha, x, ldx, gate, ld_gate, rows_per_gate,
                                static_cast<cudaStream_t>(stream));
+}
+
+int64_t tfb_tp_layout(int world, int64_t max_rows, int64_t n_cols, int64_t* offsets) {
+  if (world < 2 || world > TFB_TP_MAX_WORLD || max_rows <= 0 || n_cols <= 0 || n_cols % 32) return -1;
+  const tfb::TpLayout L = tfb::tp_layout(world, max_rows, n_cols);
+  if (offsets) {
+    offsets[0] = L.x;
+    offsets[1] = L.recv;
+    offsets[2] = L.fp;
+    offsets[3] = L.fx;
+  }
+  return L.bytes;
+}
+
+tfb_status tfb_gemm_nvfp4_tp(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* b_codes, const uint8_t* b_sf,
+                             int64_t M, int64_t N, int64_t K, float alpha, const void* gate, int64_t ld_gate,
+                             int64_t rows_per_gate, const tfb_tp_comm* comm, uint32_t epoch, void* stream) {
+  return tfb::gemm_nvfp4_tp(a_codes, a_sf, b_codes, b_sf, M, N, K, alpha, gate, ld_gate, rows_per_gate, comm, epoch,
+                            static_cast<cudaStream_t>(stream));
+}
+
+tfb_status tfb_tp_wait(const tfb_tp_comm* comm, int64_t M, int64_t N, uint32_t epoch, void* stream) {
+  return tfb::tp_wait(comm, M, N, epoch, static_cast<cudaStream_t>(stream));
 }
 
 tfb_status tfb_gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, int64_t K, const float* a_scale,

@@ -11,7 +11,8 @@
 // Work split: a CTA of 256 threads decodes a tile of 2048 values (8 super-blocks, or 64 Q8_0 blocks). The tile's
 // raw bytes (a multiple of 16 for every type) are staged in shared memory with 16-byte loads; each thread then
 // decodes 8 consecutive values and writes them with one 16-byte (f16/bf16) or two 16-byte (f32) stores, so a warp
-// writes 256 or 512 contiguous bytes. Grid-stride over tiles, up to 8 CTAs per SM. HBM-bound: per value the kernel
+// writes 256 or 512 contiguous bytes. Grid-stride over tiles, up to 8 CTAs per SM, each with the raw bytes of its
+// next two tiles in flight (register prefetch) while it decodes the current one. HBM-bound: per value the kernel
 // moves the block bytes / values (1.06 / 0.56 / 0.69 / 0.82 B for Q8_0 / Q4_K / Q5_K / Q6_K) plus the output.
 #include "tfb_common.cuh"
 
@@ -47,6 +48,17 @@ __device__ __forceinline__ float f16_at(const uint8_t* p) {
   return __half2float(__ushort_as_half(b));
 }
 
+// Exact float of a small non-negative integer (v < 2^23) on the FP32 pipe: 2^23 + v has v in its mantissa, and
+// subtracting 2^23 is exact. Same value as an int-to-float conversion, without the conversion pipe's lower rate.
+__device__ __forceinline__ float small_u2f(uint32_t v) {
+  return __fsub_rn(__uint_as_float(0x4B000000u | v), 8388608.0f);
+}
+
+// Exact float of a signed byte: (b ^ 0x80) = b + 128 as an unsigned value, then subtract 2^23 + 128.
+__device__ __forceinline__ float i8_to_f(uint32_t byte) {
+  return __fsub_rn(__uint_as_float(0x4B000000u | ((byte & 0xFFu) ^ 0x80u)), 8388736.0f);
+}
+
 // 8 bytes at an 8-byte aligned shared-memory address.
 __device__ __forceinline__ void bytes8(const uint8_t* p, uint32_t* b) {
   const uint2 w = *reinterpret_cast<const uint2*>(p);
@@ -60,11 +72,11 @@ __device__ __forceinline__ void bytes8(const uint8_t* p, uint32_t* b) {
 // Six-bit scale and min number `j` (0-7) of a K-quant block from its 12 packed bytes (ggml get_scale_min_k4).
 __device__ __forceinline__ void scale_min_k4(const uint8_t* s, int j, float& sc, float& m) {
   if (j < 4) {
-    sc = static_cast<float>(s[j] & 63);
-    m = static_cast<float>(s[j + 4] & 63);
+    sc = small_u2f(s[j] & 63);
+    m = small_u2f(s[j + 4] & 63);
   } else {
-    sc = static_cast<float>((s[j + 4] & 15) | ((s[j - 4] >> 6) << 4));
-    m = static_cast<float>((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
+    sc = small_u2f((s[j + 4] & 15) | ((s[j - 4] >> 6) << 4));
+    m = small_u2f((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
   }
 }
 
@@ -74,7 +86,7 @@ __device__ __forceinline__ void decode8(const uint8_t* blk, int o, float* y) {
   if constexpr (TYPE == TFB_GGUF_Q8_0) {
     const float d = f16_at(blk);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) y[i] = __fmul_rn(d, static_cast<float>(static_cast<int8_t>(blk[2 + o + i])));
+    for (int i = 0; i < 8; ++i) y[i] = __fmul_rn(d, i8_to_f(blk[2 + o + i]));
   } else if constexpr (TYPE == TFB_GGUF_Q4_K || TYPE == TFB_GGUF_Q5_K) {
     const int j = o >> 6, hi = (o >> 5) & 1, p = o & 31, sub = 2 * j + hi;
     float sc, m;
@@ -90,19 +102,18 @@ __device__ __forceinline__ void decode8(const uint8_t* blk, int o, float* y) {
     for (int i = 0; i < 8; ++i) {
       uint32_t v = hi ? (q[i] >> 4) : (q[i] & 15);
       if constexpr (TYPE == TFB_GGUF_Q5_K) v |= ((h[i] >> sub) & 1) << 4;
-      y[i] = __fsub_rn(__fmul_rn(ds, static_cast<float>(v)), dm);
+      y[i] = __fsub_rn(__fmul_rn(ds, small_u2f(v)), dm);
     }
   } else {  // Q6_K: half h, run r of 32 values, position p within the run
     const int h = o >> 7, r = (o >> 5) & 3, p = o & 31;
-    const int8_t sc = static_cast<int8_t>(blk[192 + 8 * h + 2 * r + (p >> 4)]);
-    const float ds = __fmul_rn(f16_at(blk + 208), static_cast<float>(sc));
+    const float ds = __fmul_rn(f16_at(blk + 208), i8_to_f(blk[192 + 8 * h + 2 * r + (p >> 4)]));
     const uint8_t* ql = blk + 64 * h + 32 * (r & 1) + p;
     const uint8_t* qh = blk + 128 + 32 * h + p;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const int lo = r < 2 ? (ql[i] & 15) : (ql[i] >> 4);
-      const int v = (lo | (((qh[i] >> (2 * r)) & 3) << 4)) - 32;
-      y[i] = __fmul_rn(ds, static_cast<float>(v));
+      const uint32_t lo = r < 2 ? (ql[i] & 15) : (ql[i] >> 4);
+      const float v = __fsub_rn(small_u2f(lo | (((qh[i] >> (2 * r)) & 3) << 4)), 32.0f);   // q - 32, exact
+      y[i] = __fmul_rn(ds, v);
     }
   }
 }
@@ -129,35 +140,54 @@ __device__ __forceinline__ void store8(void* out, int64_t idx, const float* y) {
 }
 
 template <int TYPE, int OUT>
-__global__ void __launch_bounds__(kThreads) gguf_kernel(const uint8_t* __restrict__ raw, int64_t n_blocks,
+__global__ void __launch_bounds__(kThreads, 8) gguf_kernel(const uint8_t* __restrict__ raw, int64_t n_blocks,
                                                           void* __restrict__ out) {
   using F = Fmt<TYPE>;
   constexpr int kBlocksPerTile = kTileValues / F::kValues;
   constexpr int kTileBytes = kBlocksPerTile * F::kBytes;
-  static_assert(kTileBytes % 16 == 0, "tile bytes must stage with 16-byte loads");
+  constexpr int kVecs = kTileBytes / 16;          // 16-byte pieces of a full tile: at most one per thread
+  static_assert(kTileBytes % 16 == 0 && kVecs <= kThreads, "a full tile stages with one 16-byte load per thread");
   __shared__ __align__(16) uint8_t stage[kTileBytes];
   pdl_trigger();
   pdl_wait();
   const int t = threadIdx.x;
   const int v0 = 8 * t;                 // this thread's first value within the tile
   const int blk = v0 / F::kValues;
-  for (int64_t tile = blockIdx.x; tile * kBlocksPerTile < n_blocks; tile += gridDim.x) {
+  const int64_t step = gridDim.x;
+  // The raw bytes of the next two tiles of this CTA are loaded into registers while the current tile decodes
+  // (two tiles in flight per CTA), so the HBM reads of a CTA overlap its decode and stores.
+  auto prefetch = [&](int64_t tile, uint4& r) {
+    if (t < kVecs && (tile + 1) * kBlocksPerTile <= n_blocks)
+      r = __ldg(reinterpret_cast<const uint4*>(raw + tile * kBlocksPerTile * F::kBytes) + t);
+  };
+  auto body = [&](int64_t tile, uint4& r) {
     const int64_t b0 = tile * kBlocksPerTile;
     const int nb = n_blocks - b0 < kBlocksPerTile ? static_cast<int>(n_blocks - b0) : kBlocksPerTile;
-    const uint8_t* src = raw + b0 * F::kBytes;
     if (nb == kBlocksPerTile) {
-      for (int i = t; i < kTileBytes / 16; i += kThreads)
-        reinterpret_cast<uint4*>(stage)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
-    } else {
+      if (t < kVecs) reinterpret_cast<uint4*>(stage)[t] = r;
+    } else {                            // the ragged last tile: byte loads, no prefetch
+      const uint8_t* src = raw + b0 * F::kBytes;
       for (int i = t; i < nb * F::kBytes; i += kThreads) stage[i] = __ldg(src + i);
     }
     __syncthreads();
+    prefetch(tile + 2 * step, r);
     if (blk < nb) {
       float y[8];
       decode8<TYPE>(stage + blk * F::kBytes, v0 % F::kValues, y);
       store8<OUT>(out, b0 * F::kValues + v0, y);
     }
     __syncthreads();
+  };
+  uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
+  int64_t tile = blockIdx.x;
+  prefetch(tile, r0);
+  prefetch(tile + step, r1);
+  while (tile * kBlocksPerTile < n_blocks) {
+    body(tile, r0);
+    tile += step;
+    if (tile * kBlocksPerTile >= n_blocks) break;
+    body(tile, r1);
+    tile += step;
   }
 }
 

@@ -106,6 +106,44 @@ int64_t tfb_sf_tiled_bytes(int64_t rows, int64_t k) {
   return ((rows + 127) / 128) * (k / 64) * 512;
 }
 
+tfb_status tfb_ipc_handle(const void* ptr, uint8_t* handle, int64_t* offset) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+  if (!ptr || !handle || !offset) return tfb::fail(TFB_BAD_ARG, "ipc_handle: null argument");
+  static PFN_cuMemGetAddressRange_v3020 range = nullptr;
+  if (!range) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    TFB_CUDA(cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &fn, 12000, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !fn) return tfb::fail(TFB_CUDA_ERR, "cuMemGetAddressRange unavailable");
+    range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return tfb::fail(TFB_BAD_ARG, "ipc_handle: %p is not inside a device allocation", ptr);
+  cudaIpcMemHandle_t h;
+  TFB_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+  memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+  return TFB_OK;
+}
+
+tfb_status tfb_ipc_open(const uint8_t* handle, int64_t offset, void** ptr) {
+  if (!handle || !ptr || offset < 0) return tfb::fail(TFB_BAD_ARG, "ipc_open: bad argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  TFB_CUDA(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+  *ptr = static_cast<uint8_t*>(base) + offset;
+  return TFB_OK;
+}
+
+tfb_status tfb_ipc_close(void* ptr, int64_t offset) {
+  if (!ptr || offset < 0) return tfb::fail(TFB_BAD_ARG, "ipc_close: bad argument");
+  TFB_CUDA(cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset));
+  return TFB_OK;
+}
+
 tfb_status tfb_device_status(int* code, int reset) {
   const tfb::DeviceInfo* di;
   tfb_status st = tfb::device_info(&di);

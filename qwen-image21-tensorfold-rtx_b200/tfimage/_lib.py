@@ -45,11 +45,18 @@ SIGNATURES = {
     "tfb_rms_rope_qkv": [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_float, c_vp, c_i64,
                          c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp],
     "tfb_swiglu": [c_vp, c_i64, c_i64, c_vp, c_vp],
+    "tfb_tp_layout": [c_int, c_i64, c_i64, ctypes.POINTER(c_i64)],
+    "tfb_gemm_nvfp4_tp": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_vp, c_i64, c_i64, c_vp,
+                          ctypes.c_uint32, c_vp],
+    "tfb_tp_wait": [c_vp, c_i64, c_i64, ctypes.c_uint32, c_vp],
+    "tfb_ipc_handle": [c_vp, c_vp, ctypes.POINTER(c_i64)],
+    "tfb_ipc_open": [c_vp, c_i64, ctypes.POINTER(c_vp)],
+    "tfb_ipc_close": [c_vp, c_i64],
     "tfb_gguf_block_bytes": [c_int, ctypes.POINTER(c_i64)],
     "tfb_gguf_dequant": [c_int, c_vp, c_i64, c_vp, c_int, c_vp],
 }
 RESTYPES = {"tfb_version": c_int, "tfb_last_error": ctypes.c_char_p, "tfb_sf_tiled_bytes": c_i64,
-            "tfb_gguf_block_bytes": c_i64}
+            "tfb_gguf_block_bytes": c_i64, "tfb_tp_layout": c_i64}
 
 SF_ROWS, SF_TILED = 0, 1
 GGUF_TYPES = {"Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}     # TFB_GGUF_* (ggml type ids)
@@ -294,3 +301,55 @@ def gguf_dequant(kind: str, raw, out) -> None:
         raise TfbError(f"gguf_dequant: {raw.numel()} bytes of {kind} do not hold {out.numel()} values")
     check(load().tfb_gguf_dequant(GGUF_TYPES[kind], raw.data_ptr(), out.numel(), out.data_ptr(),
                                   OUT_DTYPES[out.dtype], _stream(raw)))
+
+
+# ------------------------------------------------------------------ tensor-parallel down projection over NVLink
+TP_MAX_WORLD = 8
+
+
+class TpComm(ctypes.Structure):
+    """tfb_tp_comm: every rank's communication buffer as mapped in this process, and the shape it was laid out for."""
+    _fields_ = [("world", c_int), ("rank", c_int), ("base", c_vp * TP_MAX_WORLD), ("max_rows", c_i64),
+                ("n_cols", c_i64)]
+
+
+def tp_layout(world: int, max_rows: int, n_cols: int) -> tuple[int, list[int]]:
+    """(bytes, [x, receive slots, partial counters, x counters] offsets) of one rank's communication buffer."""
+    off = (c_i64 * 4)()
+    n = load().tfb_tp_layout(world, max_rows, n_cols, off)
+    if n < 0:
+        raise TfbError(f"tp_layout: bad arguments (world={world}, max_rows={max_rows}, n_cols={n_cols})")
+    return int(n), [int(v) for v in off]
+
+
+def ipc_handle(t: torch.Tensor) -> tuple[bytes, int]:
+    """CUDA IPC handle (64 bytes) of the allocation holding ``t`` and t's byte offset inside it."""
+    _cuda(t)
+    h = (ctypes.c_uint8 * 64)()
+    off = c_i64(0)
+    check(load().tfb_ipc_handle(t.data_ptr(), h, ctypes.byref(off)))
+    return bytes(h), int(off.value)
+
+
+def ipc_open(handle: bytes, offset: int) -> int:
+    """Maps another process's allocation into this one; returns the device address at ``offset``."""
+    h = (ctypes.c_uint8 * 64).from_buffer_copy(handle)
+    ptr = c_vp(0)
+    check(load().tfb_ipc_open(h, offset, ctypes.byref(ptr)))
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int, offset: int) -> None:
+    check(load().tfb_ipc_close(ptr, offset))
+
+
+def gemm_nvfp4_tp(a_codes, a_sf, b_codes, b_sf, M: int, N: int, K: int, alpha: float, gate: torch.Tensor,
+                  rows_per_gate: int, comm: TpComm, epoch: int) -> None:
+    _cuda(a_codes, a_sf, b_codes, b_sf, gate)
+    check(load().tfb_gemm_nvfp4_tp(a_codes.data_ptr(), a_sf.data_ptr(), b_codes.data_ptr(), b_sf.data_ptr(), M, N, K,
+                                   float(alpha), gate.data_ptr(), gate.stride(0), rows_per_gate, ctypes.byref(comm),
+                                   epoch, _stream(a_codes)))
+
+
+def tp_wait(comm: TpComm, M: int, N: int, epoch: int, device) -> None:
+    check(load().tfb_tp_wait(ctypes.byref(comm), M, N, epoch, torch.cuda.current_stream(device).cuda_stream))

@@ -283,7 +283,9 @@ class SynthMMDiT:
         cos, sin = work["rope"]
         temb = self._temb(t)
         mod = self._mod(temb, self.mod_img)
-        h = F.linear(x.flatten(2).transpose(1, 2), self.img_in).contiguous()
+        h = F.linear(x.flatten(2).transpose(1, 2), self.img_in)
+        comm = self._tp_comm(B * N)
+        h = comm.x(B * N).view(B, N, -1).copy_(h) if comm is not None else h.contiguous()
         for i, (b, (pk, pv)) in enumerate(zip(self.img_blocks, prefix.kv)):
             if work["kv"] is not None:
                 kbuf, vbuf = work["kv"][i]
@@ -341,17 +343,40 @@ class SynthMMDiT:
                 step_events[i].record()
         return x
 
-    def enable_tp(self, group=None) -> None:
+    def enable_tp(self, group=None, p2p: bool = False) -> None:
         """Single-image latency mode: split every image block's MLP over the ranks of ``group`` (gate/up columns,
-        down rows; tp.TPMLP), attention and the other linears replicated. Needs calibrated (static) scales."""
+        down rows; tp.TPMLP), attention and the other linears replicated. Needs calibrated (static) scales.
+        ``p2p``: the reduction runs inside the down GEMM over NVLink peer memory (tp.P2PComm, one per row count,
+        made collectively at the first forward), else an NCCL all-reduce follows each MLP."""
         from .tp import TPMLP
 
         for b in self.img_blocks:
             b.tp = TPMLP(b.gate_up, b.down, group)
+        self._tp = {"group": group, "p2p": p2p, "comm": None}
 
     def disable_tp(self) -> None:
         for b in self.img_blocks:
             b.tp = None
+        tp = self.__dict__.pop("_tp", None)
+        if tp and tp["comm"] is not None:
+            tp["comm"].close()
+
+    def _tp_comm(self, rows: int):
+        """The P2P communicator for ``rows`` image rows (None unless ``enable_tp(p2p=True)``); the residual stream
+        of the step lives in its buffer."""
+        from .tp import P2PComm
+
+        tp = self.__dict__.get("_tp")
+        if not tp or not tp["p2p"]:
+            return None
+        comm = tp["comm"]
+        if comm is None or comm.max_rows != rows:
+            if comm is not None:
+                comm.close()
+            comm = tp["comm"] = P2PComm(rows, self.cfg.dim, tp["group"], self.device)
+            for b in self.img_blocks:
+                b.tp.comm = comm
+        return comm
 
     # ------------------------------------------------------------------------------------------- calibration
     @torch.inference_mode()

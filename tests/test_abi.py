@@ -101,3 +101,26 @@ def test_gguf_block_table_and_host_checks():
         gguf_load.dequantize("IQ4_XS", np.zeros(136, np.uint8), (256,), "cpu")
     with pytest.raises(_lib.TfbError, match="no CPU path"):
         gguf_load.dequantize("Q4_K", og.random_blocks("Q4_K", 1, 0), (256,), "cpu")
+
+
+def test_tp_layout():
+    n, off = _lib.tp_layout(2, 4096, 3072)
+    x, recv, fp, fx = off
+    assert x == 0 and recv == 4096 * 3072 * 2                   # x: the replicated residual stream
+    assert fp - recv == 1 * 2048 * 3072 * 2                     # one receive slot of a 2048-row chunk
+    tiles = (2048 // 128) * (3072 // 256)
+    assert fx - fp == -(-tiles * 4 // 256) * 256 and n >= fx + 2 * tiles * 4
+    assert all(o % 256 == 0 for o in off)
+    n8, off8 = _lib.tp_layout(8, 4100, 3072)                    # chunks rounded up to whole 256-row tiles
+    assert off8[2] - off8[1] == 7 * 768 * 3072 * 2
+    with pytest.raises(_lib.TfbError):
+        _lib.tp_layout(1, 4096, 3072)
+    with pytest.raises(_lib.TfbError):
+        _lib.tp_layout(9, 4096, 3072)
+    assert ctypes_sizeof_comm() == 4 + 4 + 8 * 8 + 8 + 8
+
+
+def ctypes_sizeof_comm():
+    import ctypes
+
+    return ctypes.sizeof(_lib.TpComm)

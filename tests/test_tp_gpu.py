@@ -55,3 +55,97 @@ def test_tp_mlp_two_gpus(tmp_path):
         err, err_res = map(float, (tmp_path / f"rank{r}.txt").read_text().split())
         print(f"rank {r}: TP vs unsharded rel-L2 {err:.2e}, with residual {err_res:.2e}")
         assert err <= 5e-3 and err_res <= 2e-3
+
+
+def _p2p_worker(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from _helpers import bf16_cpu, f32, rel_l2
+    from tfimage import _lib
+    from tfimage import linear as L
+    from tfimage import mmdit, tp
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    lines = []
+    try:
+        M, K, F = 4096, 3072, 8192
+        x = bf16_cpu((M, K), seed=91).to(dev)
+        gu = L.Nvfp4Linear(bf16_cpu((2 * F, K), seed=92, scale=0.02).to(dev), act=float(x.float().abs().max()) / 2688)
+        down = L.Nvfp4Linear(bf16_cpu((K, F), seed=93, scale=0.02).to(dev), act=0.0008)
+        comm = tp.P2PComm(M, K)
+        fused, nccl = tp.TPMLP(gu, down, comm=comm), tp.TPMLP(gu, down)
+        ref_full = L.swiglu_mlp(gu, down, x)
+        for step in range(3):                       # three calls on one buffer: epochs 1, 2, 3
+            res = bf16_cpu((M, K), seed=94 + step, scale=3.0).to(dev)
+            gate = bf16_cpu((1, K), seed=97 + step, scale=0.5).to(dev)
+            xs = comm.x(M)
+            xs.copy_(res)
+            fused(x, residual=(xs, gate))
+            want = nccl(x, residual=(res.clone(), gate))
+            torch.cuda.synchronize()
+            same = bool(torch.equal(xs, want))
+            err = rel_l2(f32(xs), f32(res.clone().addcmul_(ref_full, gate)))
+            # every rank holds the same x
+            peer = [torch.empty_like(xs) for _ in range(world)]
+            dist.all_gather(peer, xs.clone())
+            agree = all(torch.equal(peer[0], p) for p in peer)
+            lines.append(f"mlp {int(same)} {int(agree)} {err:.3e}")
+        assert _lib.device_status() == 0
+        comm.close()
+
+        # the DiT step with the MLP split over the ranks: peer-memory reduction == NCCL all-reduce, bit for bit
+        cfg = mmdit.DitConfig(layers=2)
+        m = mmdit.SynthMMDiT(cfg, device=dev, seed=5)
+        g = torch.Generator().manual_seed(6)
+        ctx = torch.randn((1, 64, cfg.txt_dim), generator=g).to(dev)
+        noise = torch.randn((1, 64, 32, 32), generator=g).to(dev)
+        m.calibrate(ctx, noise, steps=1)
+        prefix = m.build_prefix(ctx)
+        xb = noise.to(torch.bfloat16)
+        t = torch.full((1,), 0.6, device=dev)
+        single = m.forward(xb, t, prefix, {}).clone()
+        m.enable_tp()
+        via_nccl = m.forward(xb, t, prefix, {}).clone()
+        m.disable_tp()
+        m.enable_tp(p2p=True)
+        via_p2p = [m.forward(xb, t, prefix, {}).clone() for _ in range(2)]
+        m.disable_tp()
+        torch.cuda.synchronize()
+        assert _lib.device_status() == 0
+        lines.append(f"dit {int(torch.equal(via_p2p[0], via_nccl))} {int(torch.equal(via_p2p[1], via_nccl))} "
+                     f"{rel_l2(f32(via_p2p[0]), f32(single)):.3e}")
+        with open(os.path.join(out_dir, f"p2p{rank}.txt"), "w") as fh:
+            fh.write("\n".join(lines) + "\n")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_mlp_peer_memory_two_gpus(tmp_path):
+    """The down GEMM with the cross-GPU reduction fused in (tfb_gemm_nvfp4_tp over CUDA IPC peer memory) against the
+    NCCL path: identical x on every rank, bit-equal to NCCL's bf16 all-reduce + gated residual for two ranks, over
+    repeated calls on one buffer; and the DiT step with the MLP split that way equals the NCCL-split step."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.spawn(_p2p_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        text = (tmp_path / f"p2p{r}.txt").read_text()
+        print(f"rank {r}:\n{text}")
+        for line in text.split("\n"):
+            if line.startswith("mlp"):
+                _, same, agree, err = line.split()
+                assert same == "1" and agree == "1" and float(err) <= 2e-3
+            elif line.startswith("dit"):
+                _, a, b, err = line.split()
+                # against one GPU the split step differs by the bf16 rounding of the two partials, which the next
+                # blocks' NVFP4 requantization amplifies (measured 4.8e-2 on this 2-block random-weight model, for
+                # the NCCL split as well); the bit-equality with the NCCL split is the parity check here
+                assert a == "1" and b == "1" and float(err) <= 1e-1
