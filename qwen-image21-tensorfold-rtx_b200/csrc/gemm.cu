@@ -777,7 +777,8 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
         const int owner = mb / p.tp_chunk_mb;
         const int tc = (mb - owner * p.tp_chunk_mb) * p.num_n + nb;
         if (!mbar_wait<false>(sigbar + seq % kSigSlots, (seq / kSigSlots) & 1, p.err, 0x305)) break;
-        __threadfence_system();
+        // the release add is cumulative: the peer stores the epilogue warps issued before their arrive are visible
+        // to whoever acquires the counter (a separate fence.sc.sys here cost ~10 us per launch)
         if (owner != p.tp_rank) {
           const int slot = (p.tp_rank - owner - 1 + p.tp_world) % p.tp_world;
           red_release_sys_add(reinterpret_cast<uint32_t*>(p.tp_base[owner] + p.tp_fp_off) +
