@@ -8,11 +8,13 @@
 //   Q6_K  y = (f16(d) * sc) * (q - 32)
 // then one round-to-nearest-even to the output type.
 //
-// Work split: a CTA of 256 threads decodes a tile of 2048 values (8 super-blocks, or 64 Q8_0 blocks). The tile's
+// Work split: a CTA of 256 threads decodes a tile of 4096 values (16 super-blocks, or 128 Q8_0 blocks). The tile's
 // raw bytes (a multiple of 16 for every type) are staged in shared memory with 16-byte loads; each thread then
-// decodes 8 consecutive values and writes them with one 16-byte (f16/bf16) or two 16-byte (f32) stores, so a warp
-// writes 256 or 512 contiguous bytes. Grid-stride over tiles, up to 8 CTAs per SM, each with the raw bytes of its
-// next two tiles in flight (register prefetch) while it decodes the current one. HBM-bound: per value the kernel
+// decodes 16 consecutive values -- they share one block scale (and min), so the scale unpacking is paid once per
+// 16 -- and writes them with two 16-byte (f16/bf16) or four (f32) stores. Codes become floats with one byte
+// permute + one exact FP32 add each (2^23 + code), no conversion instructions. Grid-stride over tiles, up to 4 CTAs
+// per SM, each with the raw bytes of its next two tiles in flight (register prefetch) while it decodes the current
+// one. The 8-values-per-thread version was bound by instruction issue (~22 instructions per value). Per value the kernel
 // moves the block bytes / values (1.06 / 0.56 / 0.69 / 0.82 B for Q8_0 / Q4_K / Q5_K / Q6_K) plus the output.
 #include "tfb_common.cuh"
 
@@ -22,7 +24,8 @@ namespace tfb {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kTileValues = kThreads * 8;
+constexpr int kVpt = 16;                       // values per thread: one block scale (and min) serves all 16
+constexpr int kTileValues = kThreads * kVpt;   // 4096 values per CTA tile
 
 template <int TYPE>
 struct Fmt;
@@ -44,90 +47,99 @@ struct Fmt<TFB_GGUF_Q6_K> {
 };
 
 __device__ __forceinline__ float f16_at(const uint8_t* p) {
-  const unsigned short b = static_cast<unsigned short>(p[0] | (p[1] << 8));
+  const unsigned short b = *reinterpret_cast<const unsigned short*>(p);     // 2-byte aligned in every format
   return __half2float(__ushort_as_half(b));
 }
 
-// Exact float of a small non-negative integer (v < 2^23) on the FP32 pipe: 2^23 + v has v in its mantissa, and
-// subtracting 2^23 is exact. Same value as an int-to-float conversion, without the conversion pipe's lower rate.
-__device__ __forceinline__ float small_u2f(uint32_t v) {
-  return __fsub_rn(__uint_as_float(0x4B000000u | v), 8388608.0f);
-}
-
-// Exact float of a signed byte: (b ^ 0x80) = b + 128 as an unsigned value, then subtract 2^23 + 128.
-__device__ __forceinline__ float i8_to_f(uint32_t byte) {
-  return __fsub_rn(__uint_as_float(0x4B000000u | ((byte & 0xFFu) ^ 0x80u)), 8388736.0f);
-}
-
-// 8 bytes at an 8-byte aligned shared-memory address.
-__device__ __forceinline__ void bytes8(const uint8_t* p, uint32_t* b) {
-  const uint2 w = *reinterpret_cast<const uint2*>(p);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    b[i] = (w.x >> (8 * i)) & 0xFF;
-    b[4 + i] = (w.y >> (8 * i)) & 0xFF;
-  }
+// Byte k of w as a float, exactly, with one byte permute and one FP32 add: the permute builds 0x4B0000bb = 2^23 + b
+// and subtracting `bias` (2^23 plus an offset) is exact for these small integers.
+template <int K>
+__device__ __forceinline__ float byte_f(uint32_t w, float bias) {
+  return __fsub_rn(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | K)), bias);
 }
 
 // Six-bit scale and min number `j` (0-7) of a K-quant block from its 12 packed bytes (ggml get_scale_min_k4).
 __device__ __forceinline__ void scale_min_k4(const uint8_t* s, int j, float& sc, float& m) {
+  uint32_t a, b;
   if (j < 4) {
-    sc = small_u2f(s[j] & 63);
-    m = small_u2f(s[j + 4] & 63);
+    a = s[j] & 63;
+    b = s[j + 4] & 63;
   } else {
-    sc = small_u2f((s[j + 4] & 15) | ((s[j - 4] >> 6) << 4));
-    m = small_u2f((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
+    a = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4);
+    b = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
   }
+  sc = __fsub_rn(__uint_as_float(0x4B000000u | a), 8388608.0f);
+  m = __fsub_rn(__uint_as_float(0x4B000000u | b), 8388608.0f);
 }
 
-// Values o .. o+7 (o a multiple of 8) of one block staged at `blk`.
+// 16 bytes at a 2-byte aligned shared-memory address, as 4 little-endian words.
+__device__ __forceinline__ void words16_a2(const uint8_t* p, uint32_t* w) {
+  const unsigned short* h = reinterpret_cast<const unsigned short*>(p);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) w[k] = __byte_perm(h[2 * k], h[2 * k + 1], 0x5410);
+}
+
+// Values o .. o+15 (o a multiple of 16) of one block staged at `blk`: y[i] for value o + i.
 template <int TYPE>
-__device__ __forceinline__ void decode8(const uint8_t* blk, int o, float* y) {
+__device__ __forceinline__ void decode16(const uint8_t* blk, int o, float* y) {
+  uint32_t q[4];                 // the 16 integer codes, one per byte, value i = byte i % 4 of word i / 4
+  float mul, sub = 0.0f, bias = 8388608.0f;
+  bool affine = false;           // K-quants with a min: y = ds * q - dm
   if constexpr (TYPE == TFB_GGUF_Q8_0) {
-    const float d = f16_at(blk);
+    words16_a2(blk + 2 + o, q);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) y[i] = __fmul_rn(d, i8_to_f(blk[2 + o + i]));
+    for (int k = 0; k < 4; ++k) q[k] ^= 0x80808080u;   // signed byte b -> b + 128
+    mul = f16_at(blk);
+    bias = 8388736.0f;                                // 2^23 + 128
   } else if constexpr (TYPE == TFB_GGUF_Q4_K || TYPE == TFB_GGUF_Q5_K) {
-    const int j = o >> 6, hi = (o >> 5) & 1, p = o & 31, sub = 2 * j + hi;
+    const int j = o >> 6, hi = (o >> 5) & 1, p = o & 31, sb = 2 * j + hi;
     float sc, m;
-    scale_min_k4(blk + 4, sub, sc, m);
-    const float ds = __fmul_rn(f16_at(blk), sc);
-    const float dm = __fmul_rn(f16_at(blk + 2), m);
+    scale_min_k4(blk + 4, sb, sc, m);
+    mul = __fmul_rn(f16_at(blk), sc);
+    sub = __fmul_rn(f16_at(blk + 2), m);
+    affine = true;
     constexpr int kQs = TYPE == TFB_GGUF_Q4_K ? 16 : 48;
-    uint32_t q[8];
-    bytes8(blk + kQs + 32 * j + p, q);
-    uint32_t h[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if constexpr (TYPE == TFB_GGUF_Q5_K) bytes8(blk + 16 + p, h);
+    const uint4 w = *reinterpret_cast<const uint4*>(blk + kQs + 32 * j + p);   // 16-byte aligned (144 / 176-byte blocks)
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      uint32_t v = hi ? (q[i] >> 4) : (q[i] & 15);
-      if constexpr (TYPE == TFB_GGUF_Q5_K) v |= ((h[i] >> sub) & 1) << 4;
-      y[i] = __fsub_rn(__fmul_rn(ds, small_u2f(v)), dm);
+    for (int k = 0; k < 4; ++k) q[k] = (hi ? ws[k] >> 4 : ws[k]) & 0x0F0F0F0Fu;
+    if constexpr (TYPE == TFB_GGUF_Q5_K) {
+      const uint4 h = *reinterpret_cast<const uint4*>(blk + 16 + p);          // bit sb of qh[p + i]
+      const uint32_t hs[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) q[k] |= ((hs[k] >> sb) & 0x01010101u) << 4;
     }
-  } else {  // Q6_K: half h, run r of 32 values, position p within the run
+  } else {  // Q6_K: half h, run r of 32 values, position p within the run; q - 32 through the bias
     const int h = o >> 7, r = (o >> 5) & 3, p = o & 31;
-    const float ds = __fmul_rn(f16_at(blk + 208), i8_to_f(blk[192 + 8 * h + 2 * r + (p >> 4)]));
-    const uint8_t* ql = blk + 64 * h + 32 * (r & 1) + p;
-    const uint8_t* qh = blk + 128 + 32 * h + p;
+    mul = __fmul_rn(f16_at(blk + 208),
+                    __fsub_rn(__uint_as_float(0x4B000000u | ((blk[192 + 8 * h + 2 * r + (p >> 4)] ^ 0x80u) & 0xFFu)),
+                              8388736.0f));
+    uint32_t lo[4], hb[4];
+    words16_a2(blk + 64 * h + 32 * (r & 1) + p, lo);
+    words16_a2(blk + 128 + 32 * h + p, hb);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t lo = r < 2 ? (ql[i] & 15) : (ql[i] >> 4);
-      const float v = __fsub_rn(small_u2f(lo | (((qh[i] >> (2 * r)) & 3) << 4)), 32.0f);   // q - 32, exact
-      y[i] = __fmul_rn(ds, v);
-    }
+    for (int k = 0; k < 4; ++k)
+      q[k] = ((r < 2 ? lo[k] : lo[k] >> 4) & 0x0F0F0F0Fu) | (((hb[k] >> (2 * r)) & 0x03030303u) << 4);
+    bias = 8388640.0f;                                // 2^23 + 32
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float f[4] = {byte_f<0>(q[k], bias), byte_f<1>(q[k], bias), byte_f<2>(q[k], bias), byte_f<3>(q[k], bias)};
+#pragma unroll
+    for (int b = 0; b < 4; ++b) y[4 * k + b] = affine ? __fsub_rn(__fmul_rn(mul, f[b]), sub) : __fmul_rn(mul, f[b]);
   }
 }
 
 template <int OUT>
-__device__ __forceinline__ void store8(void* out, int64_t idx, const float* y) {
+__device__ __forceinline__ void store16(void* out, int64_t idx, const float* y) {
   if constexpr (OUT == TFB_DT_F32) {
     float4* p = reinterpret_cast<float4*>(static_cast<float*>(out) + idx);
-    p[0] = make_float4(y[0], y[1], y[2], y[3]);
-    p[1] = make_float4(y[4], y[5], y[6], y[7]);
-  } else {
-    uint32_t w[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int k = 0; k < 4; ++k) p[k] = make_float4(y[4 * k], y[4 * k + 1], y[4 * k + 2], y[4 * k + 3]);
+  } else {
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
       if constexpr (OUT == TFB_DT_BF16) {
         w[i] = pack_bf16x2(y[2 * i], y[2 * i + 1]);
       } else {
@@ -135,36 +147,45 @@ __device__ __forceinline__ void store8(void* out, int64_t idx, const float* y) {
         w[i] = *reinterpret_cast<uint32_t*>(&hv);
       }
     }
-    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + idx) = make_uint4(w[0], w[1], w[2], w[3]);
+    uint4* p = reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + idx);
+    p[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    p[1] = make_uint4(w[4], w[5], w[6], w[7]);
   }
 }
 
 template <int TYPE, int OUT>
-__global__ void __launch_bounds__(kThreads, 8) gguf_kernel(const uint8_t* __restrict__ raw, int64_t n_blocks,
-                                                          void* __restrict__ out) {
+__global__ void __launch_bounds__(kThreads, 4) gguf_kernel(const uint8_t* __restrict__ raw, int64_t n_blocks,
+                                                             void* __restrict__ out) {
   using F = Fmt<TYPE>;
   constexpr int kBlocksPerTile = kTileValues / F::kValues;
   constexpr int kTileBytes = kBlocksPerTile * F::kBytes;
-  constexpr int kVecs = kTileBytes / 16;          // 16-byte pieces of a full tile: at most one per thread
-  static_assert(kTileBytes % 16 == 0 && kVecs <= kThreads, "a full tile stages with one 16-byte load per thread");
+  constexpr int kVecs = kTileBytes / 16;                      // 16-byte pieces of a full tile
+  constexpr int kLpt = (kVecs + kThreads - 1) / kThreads;     // of them per thread (1, or 2 for Q8_0)
+  static_assert(kTileBytes % 16 == 0, "a full tile stages with 16-byte loads");
   __shared__ __align__(16) uint8_t stage[kTileBytes];
   pdl_trigger();
   pdl_wait();
   const int t = threadIdx.x;
-  const int v0 = 8 * t;                 // this thread's first value within the tile
+  const int v0 = kVpt * t;              // this thread's first value within the tile
   const int blk = v0 / F::kValues;
   const int64_t step = gridDim.x;
   // The raw bytes of the next two tiles of this CTA are loaded into registers while the current tile decodes
   // (two tiles in flight per CTA), so the HBM reads of a CTA overlap its decode and stores.
-  auto prefetch = [&](int64_t tile, uint4& r) {
-    if (t < kVecs && (tile + 1) * kBlocksPerTile <= n_blocks)
-      r = __ldg(reinterpret_cast<const uint4*>(raw + tile * kBlocksPerTile * F::kBytes) + t);
+  auto prefetch = [&](int64_t tile, uint4* r) {
+    if ((tile + 1) * kBlocksPerTile <= n_blocks) {
+      const uint4* src = reinterpret_cast<const uint4*>(raw + tile * kBlocksPerTile * F::kBytes);
+#pragma unroll
+      for (int l = 0; l < kLpt; ++l)
+        if (t + l * kThreads < kVecs) r[l] = __ldg(src + t + l * kThreads);
+    }
   };
-  auto body = [&](int64_t tile, uint4& r) {
+  auto body = [&](int64_t tile, uint4* r) {
     const int64_t b0 = tile * kBlocksPerTile;
     const int nb = n_blocks - b0 < kBlocksPerTile ? static_cast<int>(n_blocks - b0) : kBlocksPerTile;
     if (nb == kBlocksPerTile) {
-      if (t < kVecs) reinterpret_cast<uint4*>(stage)[t] = r;
+#pragma unroll
+      for (int l = 0; l < kLpt; ++l)
+        if (t + l * kThreads < kVecs) reinterpret_cast<uint4*>(stage)[t + l * kThreads] = r[l];
     } else {                            // the ragged last tile: byte loads, no prefetch
       const uint8_t* src = raw + b0 * F::kBytes;
       for (int i = t; i < nb * F::kBytes; i += kThreads) stage[i] = __ldg(src + i);
@@ -172,13 +193,13 @@ __global__ void __launch_bounds__(kThreads, 8) gguf_kernel(const uint8_t* __rest
     __syncthreads();
     prefetch(tile + 2 * step, r);
     if (blk < nb) {
-      float y[8];
-      decode8<TYPE>(stage + blk * F::kBytes, v0 % F::kValues, y);
-      store8<OUT>(out, b0 * F::kValues + v0, y);
+      float y[kVpt];
+      decode16<TYPE>(stage + blk * F::kBytes, v0 % F::kValues, y);
+      store16<OUT>(out, b0 * F::kValues + v0, y);
     }
     __syncthreads();
   };
-  uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
+  uint4 r0[kLpt], r1[kLpt];
   int64_t tile = blockIdx.x;
   prefetch(tile, r0);
   prefetch(tile + step, r1);
@@ -244,7 +265,7 @@ tfb_status tfb_gguf_dequant(int type, const uint8_t* raw, int64_t n_values, void
   if (!aligned(raw, 16) || !aligned(out, 16))
     return fail(TFB_BAD_ALIGN, "gguf_dequant: raw blocks and output must be 16-byte aligned");
   if (n_values == 0) return TFB_OK;
-  const int cap = di->sm_count * 8;
+  const int cap = di->sm_count * 4;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (type) {
     case TFB_GGUF_Q8_0: return launch_type<TFB_GGUF_Q8_0>(raw, n_values, out, out_dtype, cap, s);
