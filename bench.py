@@ -390,25 +390,27 @@ def dit_leg(world: int, rank: int, dev, barrier, reduce_max) -> dict:
     # single-image latency with the MLP split over the ranks (NCCL all-reduce of the bf16 down partial per block)
     tp_lat = None
     if world > 1:
-        def tp_step_ms(p2p: bool) -> float:
+        def tp_step_ms(p2p: bool, graph: bool = False) -> float:
             model.enable_tp(p2p=p2p)
+            step = (lambda: model.step_graph(x1, t1, prefix)) if graph else (lambda: model.forward(x1, t1, prefix, work))
             for _ in range(3):
-                model.forward(x1, t1, prefix, work)
+                step()
             barrier()
             lat = [(ev(), ev()) for _ in range(10)]
             for a, b in lat:
                 a.record(stream)
-                model.forward(x1, t1, prefix, work)
+                step()
                 b.record(stream)
             barrier()
             ms = reduce_max(statistics.median(a.elapsed_time(b) for a, b in lat))
             model.disable_tp()
             return ms
 
-        tp_lat = {"world": world, "step_ms": tp_step_ms(True), "step_ms_nccl": tp_step_ms(False),
+        tp_lat = {"world": world, "step_ms": tp_step_ms(True, graph=True), "step_ms_eager": tp_step_ms(True),
+                  "step_ms_nccl": tp_step_ms(False),
                   "split": "MLP: gate/up columns (pairs kept local) and down rows over the ranks; attention, qkv, "
                            "out replicated",
-                  "collective": "step_ms: the reduction fused into the down GEMM (tfb_gemm_nvfp4_tp: partial tiles "
+                  "collective": "step_ms (one replayed CUDA graph per step; step_ms_eager: launched eagerly): the reduction fused into the down GEMM (tfb_gemm_nvfp4_tp: partial tiles "
                                 "sent to their row owner with NVLink peer stores while the GEMM runs, reduced with "
                                 "the gated residual in the owner's epilogue, x rows stored into every rank); "
                                 "step_ms_nccl: NCCL all-reduce (sum) of the bf16 down partial [4096, 3072] per block"}

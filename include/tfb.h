@@ -185,9 +185,10 @@ typedef struct {
 } tfb_tp_comm;
 
 /* Bytes of one rank's communication buffer for `world` ranks and up to max_rows x n_cols bf16 rows, and (nullable)
- * offsets[4] of its regions: x (the replicated residual stream [max_rows, n_cols] bf16, row stride n_cols), the
- * receive slots, the partial counters, the x counters. The buffer must be zero before its first use, on every rank
- * before any rank's first call; it serves one (M, N) shape until it is zeroed again. -1 on bad arguments. */
+ * offsets[5] of its regions: x (the replicated residual stream [max_rows, n_cols] bf16, row stride n_cols), the
+ * receive slots, the partial counters, the x counters, the device epoch word. The buffer must be zero before its
+ * first use, on every rank before any rank's first call; it serves one (M, N) shape until it is zeroed again. -1 on
+ * bad arguments. */
 int64_t tfb_tp_layout(int world, int64_t max_rows, int64_t n_cols, int64_t* offsets);
 
 /* x += gate * (sum over ranks of bf16(alpha * a_r @ b_r^T)), x = the comm's x region [M, N] on every rank: this
@@ -196,13 +197,19 @@ int64_t tfb_tp_layout(int world, int64_t max_rows, int64_t n_cols, int64_t* offs
  * this rank's chunk add the received partials (bf16 sum in rank order, fp32) and the gated residual
  * (bf16(fma(y, gate, x)), the arithmetic of tfb_gemm_nvfp4_resid) and are stored into every rank's x. Every rank
  * calls it with the same M, N, K, gate and epoch (1, 2, 3, ... per call on this buffer). x rows of other ranks'
- * chunks are complete only after tfb_tp_wait. Waits are bounded (TFB_DEVICE_TIMEOUT via tfb_device_status). */
+ * chunks are complete only after tfb_tp_wait. Waits are bounded (TFB_DEVICE_TIMEOUT via tfb_device_status).
+ * epoch = 0 takes the epoch from this rank's device epoch word instead (advanced by tfb_tp_advance on the same
+ * stream before each call), so that a captured CUDA graph of the calls can be replayed. */
 tfb_status tfb_gemm_nvfp4_tp(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* b_codes, const uint8_t* b_sf,
                              int64_t M, int64_t N, int64_t K, float alpha, const void* gate, int64_t ld_gate,
                              int64_t rows_per_gate, const tfb_tp_comm* comm, uint32_t epoch, void* stream);
 
-/* Enqueues a wait (bounded) until every other rank's x rows of call `epoch` are in this rank's x. */
+/* Enqueues a wait (bounded) until every other rank's x rows of call `epoch` (0: the device epoch word) are in
+ * this rank's x. */
 tfb_status tfb_tp_wait(const tfb_tp_comm* comm, int64_t M, int64_t N, uint32_t epoch, void* stream);
+
+/* Enqueues this rank's device epoch word += 1 (for the epoch = 0 form of the two calls above). */
+tfb_status tfb_tp_advance(const tfb_tp_comm* comm, void* stream);
 
 /* CUDA IPC between the processes of one node: the 64-byte handle of the device allocation holding `ptr`, and ptr's
  * offset inside it; tfb_ipc_open maps another process's allocation here (*ptr = its base + offset); tfb_ipc_close

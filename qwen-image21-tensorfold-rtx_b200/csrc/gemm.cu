@@ -98,6 +98,7 @@ struct Params {
   int tp_chunk_rows;
   int tp_tiles_chunk;    // flag slots per (sender or owner, chunk): tp_chunk_mb * num_n
   uint32_t tp_target;    // a tile's counter value once both CTAs of its group signalled this launch: CG * epoch
+  const uint32_t* tp_epoch_dev;   // non-null: the epoch is this rank's device epoch word (tfb_tp_advance)
   uint8_t* tp_base[TFB_TP_MAX_WORLD];   // every rank's communication buffer as mapped here (this rank's included)
   int64_t tp_r_off, tp_fp_off, tp_fx_off;
 };
@@ -802,6 +803,11 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
     uint64_t* xb = xbar + (warp - EPI_WARP0);
     uint32_t x_ph = 0, x_pending = 0;             // resid: parity of the next load; a load not yet waited for
     constexpr bool kResidMode = MODE == MODE_FP4_RESID || MODE == MODE_FP4_TP;
+    // TP: the counter value this launch's tiles reach (the device epoch word was written by the previous kernel
+    // of the stream, which completed before pdl_wait returned)
+    const uint32_t tp_target = MODE == MODE_FP4_TP && p.tp_epoch_dev
+                                   ? (uint32_t)CG * *reinterpret_cast<const volatile uint32_t*>(p.tp_epoch_dev)
+                                   : p.tp_target;
     int sig_seq = 0;                              // TP: tiles handed to the signal warp so far
     auto sig_hand_off = [&]() {
       // slot reuse: the signal warp has finished the tile kSigSlots back
@@ -974,7 +980,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
           if (lane == 0)
             for (int s = 0; s + 1 < p.tp_world; ++s)
               wait_counter(reinterpret_cast<const uint32_t*>(p.tp_base[p.tp_rank] + p.tp_fp_off) +
-                               (int64_t)s * p.tp_tiles_chunk + tc, p.tp_target, p.err, 0x303);
+                               (int64_t)s * p.tp_tiles_chunk + tc, tp_target, p.err, 0x303);
           __syncwarp();
         }
         // two 64-column boxes through the 128-byte-swizzled staging buffer and TMA stores (coalesced, async,
@@ -1277,7 +1283,7 @@ int64_t tp_round256(int64_t v) { return (v + 255) / 256 * 256; }
 int64_t tp_chunk_rows(int world, int64_t rows) { return ((rows + world - 1) / world + 255) / 256 * 256; }
 
 struct TpLayout {
-  int64_t chunk_rows, tiles_chunk, x, recv, fp, fx, bytes;
+  int64_t chunk_rows, tiles_chunk, x, recv, fp, fx, epoch, bytes;
 };
 
 // One rank's communication buffer: x [max_rows, n_cols] bf16 (the replicated residual stream), world-1 receive
@@ -1291,7 +1297,8 @@ TpLayout tp_layout(int world, int64_t max_rows, int64_t n_cols) {
   L.recv = tp_round256(max_rows * n_cols * 2);
   L.fp = L.recv + tp_round256((int64_t)(world - 1) * L.chunk_rows * n_cols * 2);
   L.fx = L.fp + tp_round256((int64_t)(world - 1) * L.tiles_chunk * 4);
-  L.bytes = L.fx + tp_round256((int64_t)world * L.tiles_chunk * 4);
+  L.epoch = L.fx + tp_round256((int64_t)world * L.tiles_chunk * 4);   // this rank's device epoch word
+  L.bytes = L.epoch + 256;
   return L;
 }
 
@@ -1304,16 +1311,17 @@ tfb_status tp_check(const tfb_tp_comm* c, int64_t M, int64_t N, uint32_t epoch, 
   if (M <= 0 || M > c->max_rows || N != c->n_cols)
     return fail(TFB_BAD_SHAPE, "%s: M=%lld N=%lld outside the buffer's %lld x %lld", who, (long long)M, (long long)N,
                 (long long)c->max_rows, (long long)c->n_cols);
-  if (epoch == 0 || epoch >= (1u << 27)) return fail(TFB_BAD_ARG, "%s: epoch must be in [1, 2^27)", who);
+  if (epoch >= (1u << 27)) return fail(TFB_BAD_ARG, "%s: epoch must be 0 (device epoch) or in [1, 2^27)", who);
   return TFB_OK;
 }
 
 // Waits (bounded) until every tile of every other rank's chunk has its x rows in this rank's x.
 __global__ void __launch_bounds__(256) tp_wait_kernel(const uint32_t* fx, int world, int rank, int chunk_mb,
                                                       int num_m, int num_n, int tiles_chunk, uint32_t target,
-                                                      int* err) {
+                                                      const uint32_t* epoch_dev, uint32_t cg, int* err) {
   pdl_trigger();
   pdl_wait();
+  if (epoch_dev) target = cg * *reinterpret_cast<const volatile uint32_t*>(epoch_dev);
   for (int c = 0; c < world; ++c) {
     if (c == rank) continue;
     const int mbc = max(0, min(chunk_mb, num_m - c * chunk_mb));
@@ -1322,7 +1330,24 @@ __global__ void __launch_bounds__(256) tp_wait_kernel(const uint32_t* fx, int wo
   }
 }
 
+// One thread: this rank's device epoch word += 1 (after the previous kernel of the stream completed).
+__global__ void tp_advance_kernel(uint32_t* epoch) {
+  pdl_trigger();
+  pdl_wait();
+  *epoch += 1u;
+}
+
 }  // namespace
+
+tfb_status tp_advance(const tfb_tp_comm* comm, cudaStream_t s) {
+  if (!comm || comm->world < 2 || comm->world > TFB_TP_MAX_WORLD || comm->rank < 0 || comm->rank >= comm->world ||
+      !comm->base[comm->rank])
+    return fail(TFB_BAD_ARG, "tp_advance: bad communicator");
+  const TpLayout L = tp_layout(comm->world, comm->max_rows, comm->n_cols);
+  TFB_LAUNCH(tp_advance_kernel, 1, 1, s, reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(comm->base[comm->rank]) + L.epoch));
+  TFB_CUDA(cudaGetLastError());
+  return TFB_OK;
+}
 
 tfb_status gemm_nvfp4_tp(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf, int64_t M,
                          int64_t N, int64_t K, float alpha, const void* gate, int64_t ld_gate, int64_t rows_per_gate,
@@ -1367,6 +1392,8 @@ tfb_status gemm_nvfp4_tp(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b
   p.tp_chunk_mb = p.tp_chunk_rows / (BM * cg);
   p.tp_tiles_chunk = (int)L.tiles_chunk;
   p.tp_target = (uint32_t)cg * epoch;   // one add per CTA of the tile's group
+  p.tp_epoch_dev = epoch == 0 ? reinterpret_cast<const uint32_t*>(static_cast<uint8_t*>(comm->base[comm->rank]) + L.epoch)
+                              : nullptr;
   for (int q = 0; q < comm->world; ++q) p.tp_base[q] = static_cast<uint8_t*>(comm->base[q]);
   p.tp_r_off = L.recv;
   p.tp_fp_off = L.fp;
@@ -1384,8 +1411,10 @@ tfb_status tp_wait(const tfb_tp_comm* comm, int64_t M, int64_t N, uint32_t epoch
   const int chunk_mb = (int)(tp_chunk_rows(comm->world, M) / (BM * cg));
   const int num_m = (int)((M + BM * cg - 1) / (BM * cg)), num_n = (int)((N + BN - 1) / BN);
   const uint32_t* fx = reinterpret_cast<const uint32_t*>(static_cast<uint8_t*>(comm->base[comm->rank]) + L.fx);
+  const uint32_t* ep =
+      epoch == 0 ? reinterpret_cast<const uint32_t*>(static_cast<uint8_t*>(comm->base[comm->rank]) + L.epoch) : nullptr;
   TFB_LAUNCH(tp_wait_kernel, 1, 256, s, fx, comm->world, comm->rank, chunk_mb, num_m, num_n, (int)L.tiles_chunk,
-             (uint32_t)cg * epoch, di->err_word);
+             (uint32_t)cg * epoch, ep, (uint32_t)cg, di->err_word);
   TFB_CUDA(cudaGetLastError());
   return TFB_OK;
 }
@@ -1481,8 +1510,13 @@ int64_t tfb_tp_layout(int world, int64_t max_rows, int64_t n_cols, int64_t* offs
     offsets[1] = L.recv;
     offsets[2] = L.fp;
     offsets[3] = L.fx;
+    offsets[4] = L.epoch;
   }
   return L.bytes;
+}
+
+tfb_status tfb_tp_advance(const tfb_tp_comm* comm, void* stream) {
+  return tfb::tp_advance(comm, static_cast<cudaStream_t>(stream));
 }
 
 tfb_status tfb_gemm_nvfp4_tp(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* b_codes, const uint8_t* b_sf,

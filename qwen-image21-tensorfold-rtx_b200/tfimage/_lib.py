@@ -49,6 +49,7 @@ SIGNATURES = {
     "tfb_gemm_nvfp4_tp": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_vp, c_i64, c_i64, c_vp,
                           ctypes.c_uint32, c_vp],
     "tfb_tp_wait": [c_vp, c_i64, c_i64, ctypes.c_uint32, c_vp],
+    "tfb_tp_advance": [c_vp, c_vp],
     "tfb_ipc_handle": [c_vp, c_vp, ctypes.POINTER(c_i64)],
     "tfb_ipc_open": [c_vp, c_i64, ctypes.POINTER(c_vp)],
     "tfb_ipc_close": [c_vp, c_i64],
@@ -314,8 +315,8 @@ class TpComm(ctypes.Structure):
 
 
 def tp_layout(world: int, max_rows: int, n_cols: int) -> tuple[int, list[int]]:
-    """(bytes, [x, receive slots, partial counters, x counters] offsets) of one rank's communication buffer."""
-    off = (c_i64 * 4)()
+    """(bytes, [x, receive slots, partial counters, x counters, device epoch] offsets) of one rank's buffer."""
+    off = (c_i64 * 5)()
     n = load().tfb_tp_layout(world, max_rows, n_cols, off)
     if n < 0:
         raise TfbError(f"tp_layout: bad arguments (world={world}, max_rows={max_rows}, n_cols={n_cols})")
@@ -353,3 +354,7 @@ def gemm_nvfp4_tp(a_codes, a_sf, b_codes, b_sf, M: int, N: int, K: int, alpha: f
 
 def tp_wait(comm: TpComm, M: int, N: int, epoch: int, device) -> None:
     check(load().tfb_tp_wait(ctypes.byref(comm), M, N, epoch, torch.cuda.current_stream(device).cuda_stream))
+
+
+def tp_advance(comm: TpComm, device) -> None:
+    check(load().tfb_tp_advance(ctypes.byref(comm), torch.cuda.current_stream(device).cuda_stream))

@@ -350,11 +350,14 @@ class SynthMMDiT:
         made collectively at the first forward), else an NCCL all-reduce follows each MLP."""
         from .tp import TPMLP
 
+        self.__dict__.pop("_graphs", None)           # captured steps of the other mode
         for b in self.img_blocks:
             b.tp = TPMLP(b.gate_up, b.down, group)
         self._tp = {"group": group, "p2p": p2p, "comm": None}
 
     def disable_tp(self) -> None:
+        torch.cuda.synchronize(self.device)
+        self.__dict__.pop("_graphs", None)           # graphs that reference the communicator's buffers
         for b in self.img_blocks:
             b.tp = None
         tp = self.__dict__.pop("_tp", None)

@@ -99,11 +99,15 @@ class P2PComm:
         return self.buf[o:o + rows * self.n_cols * 2].view(torch.bfloat16).view(rows, self.n_cols)
 
     def next_epoch(self, M: int, N: int) -> int:
+        """Host-side epoch of the next call (for the explicit-epoch form of the entry points)."""
+        self.check_shape(M, N)
+        self.epoch += 1
+        return self.epoch
+
+    def check_shape(self, M: int, N: int) -> None:
         if self.shape is not None and self.shape != (M, N):
             raise ValueError(f"P2PComm was used for {self.shape}; a buffer serves one shape (make another one)")
         self.shape = (M, N)
-        self.epoch += 1
-        return self.epoch
 
     def close(self) -> None:
         """Unmaps the other ranks' buffers (after this rank's last call has completed)."""
@@ -138,9 +142,12 @@ class TPMLP:
         gu = self.gate_up.lin
         f = gu.n // 2
         h_codes, h_sf = _lib.gemm_nvfp4_swiglu(q.codes, q.sf, gu.codes, gu.bs, q.m, f, gu.k, q.act * gu.scale, d.act)
-        epoch = self.comm.next_epoch(M, N)
-        _lib.gemm_nvfp4_tp(h_codes, h_sf, d.codes, d.bs, M, N, f, d.act * d.scale, g2, rows, self.comm.comm, epoch)
-        _lib.tp_wait(self.comm.comm, M, N, epoch, res.device)
+        # epochs live on the device (advanced by a kernel in stream order), so the three launches can be captured in
+        # a CUDA graph and replayed
+        self.comm.check_shape(M, N)
+        _lib.tp_advance(self.comm.comm, res.device)
+        _lib.gemm_nvfp4_tp(h_codes, h_sf, d.codes, d.bs, M, N, f, d.act * d.scale, g2, rows, self.comm.comm, 0)
+        _lib.tp_wait(self.comm.comm, M, N, 0, res.device)
         return res
 
     def __call__(self, x, residual=None) -> torch.Tensor:

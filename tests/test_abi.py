@@ -105,11 +105,12 @@ def test_gguf_block_table_and_host_checks():
 
 def test_tp_layout():
     n, off = _lib.tp_layout(2, 4096, 3072)
-    x, recv, fp, fx = off
+    x, recv, fp, fx, ep = off
     assert x == 0 and recv == 4096 * 3072 * 2                   # x: the replicated residual stream
+    assert ep > fx and n == ep + 256                            # the device epoch word
     assert fp - recv == 1 * 2048 * 3072 * 2                     # one receive slot of a 2048-row chunk
     tiles = (2048 // 128) * (3072 // 256)
-    assert fx - fp == -(-tiles * 4 // 256) * 256 and n >= fx + 2 * tiles * 4
+    assert fx - fp == -(-tiles * 4 // 256) * 256 and ep >= fx + 2 * tiles * 4
     assert all(o % 256 == 0 for o in off)
     n8, off8 = _lib.tp_layout(8, 4100, 3072)                    # chunks rounded up to whole 256-row tiles
     assert off8[2] - off8[1] == 7 * 768 * 3072 * 2

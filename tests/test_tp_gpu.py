@@ -113,11 +113,13 @@ def _p2p_worker(rank, world, port, out_dir):
         m.disable_tp()
         m.enable_tp(p2p=True)
         via_p2p = [m.forward(xb, t, prefix, {}).clone() for _ in range(2)]
+        via_graph = [m.step_graph(xb, t, prefix).clone() for _ in range(3)]   # capture, then two replays
         m.disable_tp()
         torch.cuda.synchronize()
         assert _lib.device_status() == 0
         lines.append(f"dit {int(torch.equal(via_p2p[0], via_nccl))} {int(torch.equal(via_p2p[1], via_nccl))} "
                      f"{rel_l2(f32(via_p2p[0]), f32(single)):.3e}")
+        lines.append(f"graph {int(all(torch.equal(g, via_nccl) for g in via_graph))}")
         with open(os.path.join(out_dir, f"p2p{rank}.txt"), "w") as fh:
             fh.write("\n".join(lines) + "\n")
     finally:
@@ -127,7 +129,8 @@ def _p2p_worker(rank, world, port, out_dir):
 def test_tp_mlp_peer_memory_two_gpus(tmp_path):
     """The down GEMM with the cross-GPU reduction fused in (tfb_gemm_nvfp4_tp over CUDA IPC peer memory) against the
     NCCL path: identical x on every rank, bit-equal to NCCL's bf16 all-reduce + gated residual for two ranks, over
-    repeated calls on one buffer; and the DiT step with the MLP split that way equals the NCCL-split step."""
+    repeated calls on one buffer; and the DiT step with the MLP split that way equals the NCCL-split step, eager and
+    replayed from a captured CUDA graph."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -143,6 +146,8 @@ def test_tp_mlp_peer_memory_two_gpus(tmp_path):
             if line.startswith("mlp"):
                 _, same, agree, err = line.split()
                 assert same == "1" and agree == "1" and float(err) <= 2e-3
+            elif line.startswith("graph"):
+                assert line.split()[1] == "1"        # replayed CUDA graphs of the split step (device epochs)
             elif line.startswith("dit"):
                 _, a, b, err = line.split()
                 # against one GPU the split step differs by the bf16 rounding of the two partials, which the next
