@@ -406,8 +406,9 @@ def dit_leg(world: int, rank: int, dev, barrier, reduce_max) -> dict:
             model.disable_tp()
             return ms
 
-        tp_lat = {"world": world, "step_ms": tp_step_ms(True, graph=True), "step_ms_eager": tp_step_ms(True),
-                  "step_ms_nccl": tp_step_ms(False),
+        fused = world == 2                                   # the fused path is validated for 2 ranks
+        tp_lat = {"world": world, "step_ms": tp_step_ms(True, graph=True) if fused else None,
+                  "step_ms_eager": tp_step_ms(True) if fused else None, "step_ms_nccl": tp_step_ms(False),
                   "split": "MLP: gate/up columns (pairs kept local) and down rows over the ranks; attention, qkv, "
                            "out replicated",
                   "collective": "step_ms (one replayed CUDA graph per step; step_ms_eager: launched eagerly): the reduction fused into the down GEMM (tfb_gemm_nvfp4_tp: partial tiles "
