@@ -32,8 +32,12 @@ __global__ void __launch_bounds__(kAdaThreads) adaln_kernel(const __nv_bfloat16*
   using S = AdaSplit<NCH>;
   constexpr int D = NCH * 256, WPR = S::WPR, CPT = S::CPT, RPB = S::RPB;
   __shared__ float red[2][RPB][WPR];
+  // NVFP4 multiplier per scale byte, 1 / (e4m3(sf) * g) (0 for sf = 0): scales of non-negative amax are 0..0x7E,
+  // so 128 entries cover them; one exact reciprocal per entry instead of one per 8 values
+  __shared__ float inv_tab[128];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int rib = warp / WPR, wr = warp % WPR;             // row inside the block, warp inside the row
+  if (codes && threadIdx.x < 128) inv_tab[threadIdx.x] = nvfp4_inv(threadIdx.x, nvfp4_enc(qg));
   const bool warp_live = warp < RPB * WPR;                 // WPR = 3 leaves spare warps in the block
   const int64_t row = blockIdx.x * (int64_t)RPB + rib;
   const bool live = warp_live && row < rows;
@@ -88,6 +92,9 @@ __global__ void __launch_bounds__(kAdaThreads) adaln_kernel(const __nv_bfloat16*
   const float* sc = scale + b * D;
   const float* sh = shift ? shift + b * D : nullptr;
   const Nvfp4Enc enc = nvfp4_enc(qg);
+  // this row's part of the tiled scale offset; chunk ch's word for lanes 8t adds (4 ch + t) * 512
+  const size_t sf_row = sf ? (static_cast<size_t>(row >> 7) * (D >> 6)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4
+                           : 0;
 #pragma unroll
   for (int i = 0; i < CPT; ++i) {
     const int ch = i * WPR + wr;
@@ -116,13 +123,13 @@ __global__ void __launch_bounds__(kAdaThreads) adaln_kernel(const __nv_bfloat16*
       for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(q[k]));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
       const uint32_t sfb = nvfp4_scale(amax, enc);
-      *reinterpret_cast<uint32_t*>(codes + row * (D >> 1) + (c0 >> 1)) = nvfp4_codes8(q, nvfp4_inv(sfb, enc));
+      *reinterpret_cast<uint32_t*>(codes + row * (D >> 1) + (c0 >> 1)) = nvfp4_codes8(q, inv_tab[sfb]);
       // lanes 8t, 8t+2, 8t+4, 8t+6 hold blocks 4t..4t+3 of this chunk: one 32-bit word of the tiled layout
       const uint32_t b1 = __shfl_down_sync(0xffffffffu, sfb, 2);
       const uint32_t b2 = __shfl_down_sync(0xffffffffu, sfb, 4);
       const uint32_t b3 = __shfl_down_sync(0xffffffffu, sfb, 6);
       if ((lane & 7) == 0)
-        *reinterpret_cast<uint32_t*>(sf + sf_tiled_offset(row, ch * 16 + (lane >> 1), D >> 6)) =
+        *reinterpret_cast<uint32_t*>(sf + sf_row + (size_t)(ch * 4 + (lane >> 3)) * 512) =
             sfb | (b1 << 8) | (b2 << 16) | (b3 << 24);
     }
   }
