@@ -519,12 +519,12 @@ def run_ours(args):
               for _ in range(max(3, min(args.steps, 50)))]
     # the public host-buffer call: rows streamed in chunks, copies in both directions overlapped with the MLP
     for _ in range(2):
-        L.swiglu_mlp_host(gate_up, down, x_host, y_host, chunks=8, graph=True)
+        L.swiglu_mlp_host(gate_up, down, x_host, y_host, chunks=M_ROWS // 256, graph=True)
     barrier()
     for a, b in e2e_ev:
         flush.zero_()
         a.record(stream)
-        L.swiglu_mlp_host(gate_up, down, x_host, y_host, chunks=8, graph=True)
+        L.swiglu_mlp_host(gate_up, down, x_host, y_host, chunks=M_ROWS // 256, graph=True)
         b.record(stream)
     barrier()
     e2e_t = torch.tensor([sum(a.elapsed_time(b) for a, b in e2e_ev) / len(e2e_ev)], dtype=torch.float64,

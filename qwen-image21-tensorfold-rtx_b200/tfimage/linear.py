@@ -289,7 +289,8 @@ def _mlp_host_pipeline(gate_up, down, x_host, y_host, xd, chunks: int) -> bool:
     s_in, s_out = _COPY_STREAMS[dev]
     cur = torch.cuda.current_stream(dev)
     M = x_host.shape[0]
-    step = max(256, -(-M // chunks + 255) // 256 * 256)          # whole 256-row pair tiles per chunk
+    per = -(-M // chunks)                                         # ceil(M / chunks) rows ...
+    step = max(256, -(-per // 256) * 256)                          # ... rounded up to whole 256-row pair tiles
     s_in.wait_stream(cur)
     s_out.wait_stream(cur)
     for r0 in range(0, M, step):
