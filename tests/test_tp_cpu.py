@@ -7,6 +7,7 @@ import os
 import socket
 
 import numpy as np
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -93,3 +94,23 @@ def test_shards_reassemble_the_unsharded_containers():
         ds_ = [tp.shard_down(dn, r, world) for r in range(world)]
         assert torch.equal(torch.cat([s.codes for s in ds_], 1), dn.codes)
         assert torch.equal(torch.cat([s.scales().view(torch.uint8) for s in ds_], 1), dn.scales().view(torch.uint8))
+
+
+def test_p2p_comm_refuses_unvalidated_group_sizes(tmp_path):
+    """The fused peer-memory path is validated for 2 ranks: a group of another size is refused before any buffer is
+    made (checked with a 1-rank gloo group, no GPU involved)."""
+    import socket
+
+    import torch.distributed as dist
+
+    from tfimage import tp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    try:
+        with pytest.raises(ValueError, match="2 ranks"):
+            tp.P2PComm(4096, 3072)
+    finally:
+        dist.destroy_process_group()
