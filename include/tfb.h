@@ -95,6 +95,19 @@ tfb_status tfb_gemm_nvfp4_resid(const uint8_t* a_codes, const uint8_t* a_sf, con
                                 const uint8_t* b_sf, int64_t M, int64_t N, int64_t K, float alpha, void* x,
                                 int64_t ldx, const void* gate, int64_t ld_gate, int64_t rows_per_gate, void* stream);
 
+/* The attention input projection with the block's q / k RMSNorm + RoPE and the v copy in the epilogue: for rows
+ * m = b * ntok + n of a_codes [B * ntok, K/2] and W_qkv codes [3 * H * 128, K/2], the GEMM output (bf16(alpha * acc),
+ * the reference's qkv tensor) of q and k heads is normalised and rotated with the arithmetic of tfb_rms_rope_qkv
+ * (weights wq / wk fp32 [128], cos / sin fp32 [ntok, 64] of the image tokens) and v is copied; each part goes to
+ * its destination + b * *_sb + n * *_sn + h * 128 (element strides; k and v typically behind a kept prefix).
+ * Replaces the reference block's qkv linear + two rms_rope calls + the v copy (tfimage/qwen_image21.py:176-191);
+ * bit-equal to tfb_gemm_nvfp4 followed by tfb_rms_rope_qkv. ntok % 32 == 0, K % 128 == 0. */
+tfb_status tfb_gemm_nvfp4_qkv(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* b_codes,
+                              const uint8_t* b_sf, int64_t B, int64_t ntok, int64_t H, int64_t K, float alpha,
+                              const float* wq, const float* wk, const float* cos, const float* sin, float eps, void* q,
+                              int64_t q_sb, int64_t q_sn, void* k, int64_t k_sb, int64_t k_sn, void* v, int64_t v_sb,
+                              int64_t v_sn, void* stream);
+
 /* Gate/up NVFP4 GEMM with a SwiGLU epilogue that writes NVFP4: W_gu = [gate; up] codes [2F, K].
  * h = bf16(bf16(silu(gate)) * up) with gate/up = bf16(alpha * acc), quantized under h_global into
  * h_codes [M, F/2] and h_sf (TFB_SF_TILED, rows = M, K = F). gu_out and h_out (both nullable) receive the

@@ -148,25 +148,16 @@ void launch_adaln(const void* x, int64_t rows, int64_t rows_total, int64_t rows_
 // One lane's 8 elements of a head: RMSNorm over the half-warp's 128 (weight w), then RoPE on the pairs.
 __device__ __forceinline__ uint4 rms_rope_piece(uint4 raw, const float* __restrict__ w, int l, const float* cv,
                                                 const float* sv, float eps) {
-  constexpr int D = 128;
   float x[8];
   unpack_bf16x8(raw, x);
-  float ss = 0.0f;
+  float ss = sumsq8(x);
 #pragma unroll
-  for (int k = 0; k < 8; ++k) ss += x[k] * x[k];
-#pragma unroll
-  for (int o = 8; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float rr = rsqrtf(ss / D + eps);
+  for (int o = 8; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+  const float rr = rms_rr(ss, eps);
   const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + l * 8));
   const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + l * 8 + 4));
   const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-  uint32_t o[4];
-#pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const float x0 = x[2 * p] * rr * wv[2 * p], x1 = x[2 * p + 1] * rr * wv[2 * p + 1];
-    o[p] = pack_bf16x2(cv[p] * x0 - sv[p] * x1, sv[p] * x0 + cv[p] * x1);
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
+  return norm_rope8(x, rr, wv, cv, sv);
 }
 
 __global__ void __launch_bounds__(256) rms_rope_kernel(const __nv_bfloat16* __restrict__ src, int64_t units, int64_t N,

@@ -64,7 +64,10 @@ constexpr uint32_t SF_STAGE_COLS = 48;
 // x = bf16(fma(bf16(sum over ranks of the partials), gate, x)), and stores the new x rows locally and into every
 // other rank's x (again with a per-tile counter). Tiles of other ranks' chunks go first, so by the time a rank
 // reaches its own chunk the partials for it have been sent a wave of tiles earlier.
-enum Mode { MODE_FP4 = 0, MODE_FP8 = 1, MODE_FP4_SWIGLU = 2, MODE_FP4_RESID = 3, MODE_FP4_TP = 4 };
+// MODE_FP4_QKV: the attention input projection with the reference block's RMSNorm + RoPE of q and k (and the v
+// copy behind the kept prefix) in the epilogue: every 128-column half of a 256-column tile is one head of one of
+// q / k / v (H * 128 columns each), one epilogue thread holds one head row, so the row's norm needs no exchange.
+enum Mode { MODE_FP4 = 0, MODE_FP8 = 1, MODE_FP4_SWIGLU = 2, MODE_FP4_RESID = 3, MODE_FP4_TP = 4, MODE_FP4_QKV = 5 };
 
 struct Params {
   int M, N;              // output rows / cols (swiglu: N = F, the hidden width)
@@ -101,6 +104,14 @@ struct Params {
   const uint32_t* tp_epoch_dev;   // non-null: the epoch is this rank's device epoch word (tfb_tp_advance)
   uint8_t* tp_base[TFB_TP_MAX_WORLD];   // every rank's communication buffer as mapped here (this rank's included)
   int64_t tp_r_off, tp_fp_off, tp_fx_off;
+  // MODE_FP4_QKV: rows m = b * qk_ntok + n; outputs part p in {q, k, v} at dst[p] + b * sb[p] + n * sn[p] + h * 128
+  int qk_heads, qk_ntok;
+  __nv_bfloat16* qk_dst[3];
+  int64_t qk_sb[3], qk_sn[3];
+  const float* qk_w[2];          // RMSNorm weights of q and k, fp32 [128]
+  const float* qk_cos;           // fp32 [qk_ntok, 64]
+  const float* qk_sin;
+  float qk_eps;
 };
 
 // ----------------------------------------------------------------------------------------------- PTX wrappers
@@ -943,6 +954,74 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
           if (CG == 2 && rank != 0) mbar_arrive_cluster(acc_empty_l);
           else mbar_arrive(acc_empty);
         }
+        if constexpr (MODE == MODE_FP4_QKV) {
+          // this warp's 128 columns are head `head` of part q / k / v; thread = one row of it
+          const int HD = p.qk_heads * 128;
+          const int part = n_base / HD, head = (n_base - part * HD) >> 7;
+          const int grow0 = row0 + q * 32;                   // qk_ntok % 32 == 0: the 32 rows share a batch
+          const int bb = grow0 / p.qk_ntok, n0 = grow0 - bb * p.qk_ntok;
+          const bool norm = part < 2 && m < p.M;
+          float rr = 0.0f;
+          if (norm) {
+            // RMSNorm statistics over the head row from the bf16 GEMM outputs (the reference's qkv tensor): 16
+            // partial sums of 8, added in the butterfly order of the standalone kernel's 16-lane reduction
+            float a8[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float x[8], y[8];
+              unpack_bf16x8(make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]), x);
+              unpack_bf16x8(make_uint4(pk[32 + 4 * j], pk[33 + 4 * j], pk[34 + 4 * j], pk[35 + 4 * j]), y);
+              a8[j] = __fadd_rn(sumsq8(x), sumsq8(y));
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) a8[j] = __fadd_rn(a8[j], a8[j + 4]);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) a8[j] = __fadd_rn(a8[j], a8[j + 2]);
+            rr = rms_rr(__fadd_rn(a8[0], a8[1]), p.qk_eps);
+          }
+          __nv_bfloat16* dst = p.qk_dst[part] + (int64_t)bb * p.qk_sb[part] + (int64_t)head * 128;
+          const float* w = p.qk_w[part < 2 ? part : 0];
+          const float* cs = p.qk_cos + (int64_t)(n0 + lane) * 64;
+          const float* sn = p.qk_sin + (int64_t)(n0 + lane) * 64;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            __syncwarp();
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch)
+              *reinterpret_cast<uint4*>(stg + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
+                  make_uint4(pk[c * 32 + 4 * ch], pk[c * 32 + 4 * ch + 1], pk[c * 32 + 4 * ch + 2],
+                             pk[c * 32 + 4 * ch + 3]);
+            if (norm) {
+              // weight and RoPE on this thread's row of the box, 8 values at a time, in place in shared memory
+#pragma unroll 1
+              for (int j = 0; j < 8; ++j) {
+                uint4* px = reinterpret_cast<uint4*>(stg + lane * 128 + ((j ^ (lane & 7)) << 4));
+                float x[8];
+                unpack_bf16x8(*px, x);
+                const int jj = c * 8 + j;
+                const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + jj * 8));
+                const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + jj * 8 + 4));
+                const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + jj * 4));
+                const float4 s4 = __ldg(reinterpret_cast<const float4*>(sn + jj * 4));
+                const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+                *px = norm_rope8(x, rr, wv, cv, sv);
+              }
+            }
+            __syncwarp();
+            // coalesced 16-byte stores, 4 rows x 128 B per pass, into the part's destination rows
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int rr2 = i * 4 + (lane >> 3), ck = lane & 7;
+              if (grow0 + rr2 < p.M && n_base + c * 64 < p.N)
+                *reinterpret_cast<uint4*>(dst + (int64_t)(n0 + rr2) * p.qk_sn[part] + c * 64 + ck * 8) =
+                    *reinterpret_cast<const uint4*>(stg + rr2 * 128 + ((ck ^ (rr2 & 7)) << 4));
+            }
+          }
+          __syncwarp();
+          acc_ph ^= 1;
+          continue;
+        }
         if constexpr (MODE == MODE_FP4_TP) {
           if (owner != p.tp_rank) {
             // another rank's rows: this rank's bf16 partial goes to the owner's receive slot for this sender,
@@ -1419,6 +1498,58 @@ tfb_status tp_wait(const tfb_tp_comm* comm, int64_t M, int64_t N, uint32_t epoch
   return TFB_OK;
 }
 
+tfb_status gemm_nvfp4_qkv(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf, int64_t B,
+                          int64_t ntok, int64_t H, int64_t K, float alpha, const float* wq, const float* wk,
+                          const float* cosp, const float* sinp, float eps, void* const dst[3], const int64_t sb[3],
+                          const int64_t sn[3], cudaStream_t s) {
+  const int64_t M = B * ntok, N = 3 * H * 128;
+  tfb_status st = check_common(M, N, K, "gemm_nvfp4_qkv");
+  if (st != TFB_OK) return st;
+  if (B < 0 || ntok <= 0 || ntok % 32 || H <= 0)
+    return fail(TFB_BAD_SHAPE, "gemm_nvfp4_qkv: need ntok %% 32 == 0 and H > 0 (B=%lld ntok=%lld H=%lld)",
+                (long long)B, (long long)ntok, (long long)H);
+  if (!wq || !wk || !cosp || !sinp || !aligned(wq, 16) || !aligned(wk, 16) || !aligned(cosp, 16) || !aligned(sinp, 16) ||
+      !aligned(a_sf, 16) || !aligned(b_sf, 16))
+    return fail(TFB_BAD_ALIGN, "gemm_nvfp4_qkv: weights, cos/sin tables and scales must be 16-byte aligned");
+  for (int i = 0; i < 3; ++i)
+    if (!dst[i] || !aligned(dst[i], 16) || sb[i] % 8 || sn[i] % 8 || sn[i] < H * 128)
+      return fail(TFB_BAD_ALIGN, "gemm_nvfp4_qkv: destination %d needs 16-byte alignment, strides %% 8 == 0 and a row "
+                  "stride >= H * 128", i);
+  const DeviceInfo* di;
+  if ((st = device_info(&di)) != TFB_OK) return st;
+  if (M == 0) return TFB_OK;
+  CUtensorMap ta, tb, ty;
+  if ((st = make_tmap_u8(&ta, a, K / 2, M, K / 2, BKB, BM)) != TFB_OK) return st;
+  if ((st = make_tmap_u8(&tb, b, K / 2, N, K / 2, BKB, 128)) != TFB_OK) return st;
+  // (the epilogue stores through its own row addressing; this map is a placeholder over the q destination)
+  if ((st = make_tmap_2d(&ty, dst[0], 2, H * 128, ntok, sn[0] * 2, 64, 32, true)) != TFB_OK) return st;
+  Params p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.num_ks = (int)(K / 256 + (K % 256 ? 1 : 0));
+  p.kb_total = (int)(K / 64);
+  p.b_rows = (int)N;
+  p.sfa = a_sf;
+  p.sfb = b_sf;
+  p.sf_chunks = (int)(K / 64);
+  p.sfb_groups = (int)((N + 127) / 128);
+  p.alpha = alpha;
+  p.err = di->err_word;
+  p.qk_heads = (int)H;
+  p.qk_ntok = (int)ntok;
+  for (int i = 0; i < 3; ++i) {
+    p.qk_dst[i] = static_cast<__nv_bfloat16*>(dst[i]);
+    p.qk_sb[i] = sb[i];
+    p.qk_sn[i] = sn[i];
+  }
+  p.qk_w[0] = wq;
+  p.qk_w[1] = wk;
+  p.qk_cos = cosp;
+  p.qk_sin = sinp;
+  p.qk_eps = eps;
+  return dispatch<MODE_FP4_QKV>(ta, tb, ty, p, M, BN, N, s);
+}
+
 tfb_status gemm_nvfp4_swiglu(const uint8_t* a, const uint8_t* a_sf, const uint8_t* gu, const uint8_t* gu_sf, int64_t M,
                              int64_t F, int64_t K, float alpha, float h_g, uint8_t* h_codes, uint8_t* h_sf,
                              void* gu_out, void* h_out, cudaStream_t s) {
@@ -1528,6 +1659,17 @@ tfb_status tfb_gemm_nvfp4_tp(const uint8_t* a_codes, const uint8_t* a_sf, const 
 
 tfb_status tfb_tp_wait(const tfb_tp_comm* comm, int64_t M, int64_t N, uint32_t epoch, void* stream) {
   return tfb::tp_wait(comm, M, N, epoch, static_cast<cudaStream_t>(stream));
+}
+
+tfb_status tfb_gemm_nvfp4_qkv(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* b_codes,
+                              const uint8_t* b_sf, int64_t B, int64_t ntok, int64_t H, int64_t K, float alpha,
+                              const float* wq, const float* wk, const float* cos, const float* sin, float eps, void* q,
+                              int64_t q_sb, int64_t q_sn, void* k, int64_t k_sb, int64_t k_sn, void* v, int64_t v_sb,
+                              int64_t v_sn, void* stream) {
+  void* const dst[3] = {q, k, v};
+  const int64_t sb[3] = {q_sb, k_sb, v_sb}, sn[3] = {q_sn, k_sn, v_sn};
+  return tfb::gemm_nvfp4_qkv(a_codes, a_sf, b_codes, b_sf, B, ntok, H, K, alpha, wq, wk, cos, sin, eps, dst, sb, sn,
+                             static_cast<cudaStream_t>(stream));
 }
 
 tfb_status tfb_gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, int64_t K, const float* a_scale,

@@ -153,4 +153,29 @@ __device__ __forceinline__ void unpack_bf16x8(const uint4& u, float* f) {
   }
 }
 
+// RMSNorm over a 128-wide head + RoPE on interleaved pairs, shared by the standalone kernel (16 lanes x 8 values per
+// head row) and the qkv GEMM epilogue (one thread per head row), so both produce the same bits. Every rounding is
+// spelled out (no compiler contraction choices): the sum of squares of 8 values is a chain of fused multiply-adds
+// from 0; the 16 such partial sums of a row are added in the xor-butterfly order of a 16-lane shuffle reduction.
+__device__ __forceinline__ float sumsq8(const float* x) {
+  float ss = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) ss = __fmaf_rn(x[k], x[k], ss);
+  return ss;
+}
+__device__ __forceinline__ float rms_rr(float ss, float eps) { return rsqrtf(__fadd_rn(__fmul_rn(ss, 0.0078125f), eps)); }
+// 8 values (4 pairs) normalised by rr, scaled by w, rotated by (c, s): (c x0 - s x1, s x0 + c x1), to bf16.
+__device__ __forceinline__ uint4 norm_rope8(const float* x, float rr, const float* wv, const float* cv,
+                                            const float* sv) {
+  uint32_t o[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float x0 = __fmul_rn(__fmul_rn(x[2 * p], rr), wv[2 * p]);
+    const float x1 = __fmul_rn(__fmul_rn(x[2 * p + 1], rr), wv[2 * p + 1]);
+    o[p] = pack_bf16x2(__fmaf_rn(cv[p], x0, -__fmul_rn(sv[p], x1)), __fmaf_rn(sv[p], x0, __fmul_rn(cv[p], x1)));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+
 }  // namespace tfb

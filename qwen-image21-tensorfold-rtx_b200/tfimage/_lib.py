@@ -45,6 +45,8 @@ SIGNATURES = {
     "tfb_rms_rope_qkv": [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_float, c_vp, c_i64,
                          c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp],
     "tfb_swiglu": [c_vp, c_i64, c_i64, c_vp, c_vp],
+    "tfb_gemm_nvfp4_qkv": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_float, c_vp, c_vp, c_vp, c_vp, c_float,
+                           c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp],
     "tfb_tp_layout": [c_int, c_i64, c_i64, ctypes.POINTER(c_i64)],
     "tfb_gemm_nvfp4_tp": [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_float, c_vp, c_i64, c_i64, c_vp,
                           ctypes.c_uint32, c_vp],
@@ -191,6 +193,17 @@ def gemm_nvfp4_resid(a_codes, a_sf, b_codes, b_sf, M: int, N: int, K: int, alpha
                                       K, float(alpha), x.data_ptr(), x.stride(0), gate.data_ptr(), gate.stride(0),
                                       int(rows_per_gate), _stream(x)))
     return x
+
+
+def gemm_nvfp4_qkv(a_codes, a_sf, b_codes, b_sf, B: int, ntok: int, H: int, K: int, alpha: float, wq, wk, cos, sin,
+                   eps: float, q, k, v) -> None:
+    """qkv GEMM with q / k RMSNorm + RoPE and the v copy in the epilogue; q, k, v [B, ntok, H, 128] views (rows of
+    H * 128 contiguous)."""
+    _cuda(a_codes, a_sf, b_codes, b_sf, wq, wk, cos, sin, q, k, v)
+    check(load().tfb_gemm_nvfp4_qkv(a_codes.data_ptr(), a_sf.data_ptr(), b_codes.data_ptr(), b_sf.data_ptr(), B, ntok,
+                                    H, K, float(alpha), wq.data_ptr(), wk.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                                    float(eps), q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0),
+                                    k.stride(1), v.data_ptr(), v.stride(0), v.stride(1), _stream(a_codes)))
 
 
 def gemm_fp8(a8, b8, M: int, N: int, K: int, a_scale, b_scale, out=None) -> torch.Tensor:

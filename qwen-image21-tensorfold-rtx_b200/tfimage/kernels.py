@@ -67,6 +67,30 @@ def rms_rope_qkv(src: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, cos: tor
     _lib.rms_rope_qkv(src, f(wq), f(wk), f(cos), f(sin), eps, q, k, v)
 
 
+def qkv_rms_rope(qkv_linear, x, wq: torch.Tensor, wk: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, eps: float,
+                 q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> bool:
+    """This build's addition: ``rms_rope_qkv(qkv_linear(x).view(B, N, 3, H, D), ...)`` with the normalisation,
+    rotation and v copy in the qkv GEMM's epilogue (no qkv tensor in HBM), bit-equal to the two-step form. x: the
+    [B, N, dim] bf16 rows or their ``Nvfp4Act`` (e.g. from ``adaln(quant=)``); q, k, v as in ``rms_rope_qkv``.
+    False (nothing done) when the layer is not a static-scale NVFP4 linear, D != 128 or N % 32 != 0."""
+    from .linear import Nvfp4Act, Nvfp4Linear
+
+    B, N, H, D = q.shape
+    if not isinstance(qkv_linear, Nvfp4Linear) or qkv_linear.dynamic or D != 128 or N % 32:
+        return False
+    for t in (q, k, v):
+        if t.stride(-1) != 1 or t.stride(-2) != D or tuple(t.shape) != (B, N, H, D):
+            raise _lib.TfbError("qkv_rms_rope: destinations need contiguous [H, D] rows")
+    lin = qkv_linear.lin
+    if lin.n != 3 * H * D:
+        raise _lib.TfbError(f"qkv_rms_rope: the layer has {lin.n} outputs, not 3 x {H} x {D}")
+    a = x if isinstance(x, Nvfp4Act) else qkv_linear.quantize(x.reshape(B * N, -1))
+    f = lambda t: t.float().contiguous()   # noqa: E731
+    _lib.gemm_nvfp4_qkv(a.codes, a.sf, lin.codes, lin.bs, B, N, H, lin.k, a.act * lin.scale, f(wq), f(wk), f(cos),
+                        f(sin), eps, q, k, v)
+    return True
+
+
 def swiglu(gu: torch.Tensor) -> torch.Tensor:
     """kernels.py:84-92: [M, 2F] = [gate | up] bf16 -> silu(gate) * up, [M, F] bf16."""
 

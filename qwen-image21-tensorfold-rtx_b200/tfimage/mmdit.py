@@ -181,14 +181,15 @@ class SynthMMDiT:
         a_in = K.adaln(x, sc1, eps, shift=sh1, quant=b.qkv if static else None, out=bf() if static else None)
         if not static:
             a_in = a_in.reshape(B * N, -1)
-        qkv = b.qkv(a_in).view(B, N, 3, H, Dh)
         q = torch.empty((B, N, H, Dh), dtype=torch.bfloat16, device=x.device)
-        K.rms_rope_qkv(qkv, b.norm_q, b.norm_k, cos, sin, eps, q, kbuf[:, P:], vbuf[:, P:])
+        if rec or not K.qkv_rms_rope(b.qkv, a_in, b.norm_q, b.norm_k, cos, sin, eps, q, kbuf[:, P:], vbuf[:, P:]):
+            qkv = b.qkv(a_in).view(B, N, 3, H, Dh)    # record mode keeps the qkv tensor for the tests
+            K.rms_rope_qkv(qkv, b.norm_q, b.norm_k, cos, sin, eps, q, kbuf[:, P:], vbuf[:, P:])
         o = _sdpa(q.transpose(1, 2), kbuf.transpose(1, 2), vbuf.transpose(1, 2), causal)
         o = o.transpose(1, 2)
         if rec:                       # the branch output on its own, then torch's addcmul_ (tests)
             a = b.out(o.reshape(B * N, H * Dh)).view(B, N, -1)
-            record.update(a_in=a_in, qkv=qkv, q=q, o=o, att=a, x_in=x.clone())
+            record.update(a_in=a_in, qkv=qkv, q=q, o=o, att=a, x_in=x.clone())   # (rec: qkv set above)
             x.addcmul_(a, g1)
         else:                         # x += g1 * out(o), in the out GEMM's epilogue for NVFP4 layers
             L.gated_residual_(b.out, o.reshape(B * N, H * Dh), x, g1)

@@ -127,3 +127,32 @@ def test_rms_rope_qkv_matches_per_part_kernel(dev, B, N, H):
     assert torch.equal(q, q_ref) and torch.equal(kbuf[:, P:], k_ref)
     assert torch.equal(vbuf[:, P:], qkv[:, :, 2])
     assert bool((kbuf[:, :P] == 7.0).all()) and bool((vbuf[:, :P] == -3.0).all())
+
+
+@pytest.mark.parametrize("B,N,H", [(1, 4096, 24), (2, 96, 24), (3, 64, 5)])
+def test_qkv_gemm_with_rms_rope_epilogue_matches_two_steps(dev, B, N, H):
+    """tfb_gemm_nvfp4_qkv (the qkv GEMM with q / k RMSNorm + RoPE and the v copy in its epilogue) equals the qkv GEMM
+    followed by tfb_rms_rope_qkv bit for bit, writes k / v behind a kept prefix without touching it; odd head counts
+    put q / k / v boundaries inside a 256-column tile."""
+    from tfimage import linear as L
+
+    D, P, Kd = 128, 64, 3072
+    x = bf16_cpu((B * N, Kd), seed=B * N + H).to(dev)
+    g = torch.Generator().manual_seed(73)
+    lin = L.Nvfp4Linear((torch.randn(3 * H * D, Kd, generator=g) * 0.02).to(torch.bfloat16).to(dev),
+                        act=float(x.float().abs().max()) / 2688)
+    wq, wk = (torch.randn(D, generator=g) * 0.05 + 1).to(dev), (torch.randn(D, generator=g) * 0.05 + 1).to(dev)
+    cos, sin = ofu.rope_table(np.concatenate([ofu.text_ids(P), ofu.image_ids(1, N, P, (1, N))])[P:])
+    cs, sn = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    qkv = lin(x).view(B, N, 3, H, D)
+    q_ref = torch.empty((B, N, H, D), dtype=torch.bfloat16, device=dev)
+    kb_ref = torch.full((B, P + N, H, D), 7.0, dtype=torch.bfloat16, device=dev)
+    vb_ref = torch.full_like(kb_ref, -3.0)
+    K.rms_rope_qkv(qkv, wq, wk, cs, sn, 1e-6, q_ref, kb_ref[:, P:], vb_ref[:, P:])
+    q = torch.empty_like(q_ref)
+    kbuf = torch.full_like(kb_ref, 7.0)
+    vbuf = torch.full_like(kb_ref, -3.0)
+    assert K.qkv_rms_rope(lin, x.view(B, N, Kd), wq, wk, cs, sn, 1e-6, q, kbuf[:, P:], vbuf[:, P:])
+    torch.cuda.synchronize()
+    assert torch.equal(q, q_ref)
+    assert torch.equal(kbuf, kb_ref) and torch.equal(vbuf, vb_ref)
