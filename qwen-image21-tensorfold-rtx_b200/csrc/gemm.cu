@@ -852,7 +852,10 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
         // this warp: hidden columns [half*64, half*64 + 64) of the tile = gate and up accumulator columns
         const int F = p.N;
         const int64_t col0 = (int64_t)nb * 128 + half * 64;
-        uint32_t hp[32];                           // 64 bf16 h values, packed in pairs
+        // drain first, release, then compute: the accumulator goes to bf16 pairs (gate and up, 64 registers) and is
+        // handed back to the MMA thread before the SwiGLU math, so the next tile's MMAs start after the TMEM reads
+        // alone (the math, ~2 us of a tile, overlaps them)
+        uint32_t hp[32], upk[32];                  // gate pairs, then h pairs in place; up pairs
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t raw[32];                        // [0, 16): gate, [16, 32): up -- 16 hidden columns
@@ -861,22 +864,9 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
           for (int j = 0; j < 16; j += 2) {
             // every bf16 rounding goes through the paired converter (one cvt.rn.bf16x2 per two values): single-
             // value conversions made this loop ~13 % of the whole GEMM's time, as much as the silu itself
-            const uint32_t gp = pack_bf16x2(__uint_as_float(raw[j]) * p.alpha, __uint_as_float(raw[j + 1]) * p.alpha);
-            const uint32_t up =
+            hp[c * 8 + j / 2] = pack_bf16x2(__uint_as_float(raw[j]) * p.alpha, __uint_as_float(raw[j + 1]) * p.alpha);
+            upk[c * 8 + j / 2] =
                 pack_bf16x2(__uint_as_float(raw[16 + j]) * p.alpha, __uint_as_float(raw[16 + j + 1]) * p.alpha);
-            const uint32_t sp = pack_bf16x2(silu_fast(__uint_as_float(gp << 16)), silu_fast(__uint_as_float(gp & 0xFFFF0000u)));
-            hp[c * 8 + j / 2] = pack_bf16x2(__uint_as_float(sp << 16) * __uint_as_float(up << 16),
-                                            __uint_as_float(sp & 0xFFFF0000u) * __uint_as_float(up & 0xFFFF0000u));
-          }
-          if (p.gu_out && m < p.M) {              // test-only output: the bf16 gate/up values the math used
-            __nv_bfloat16* dg = p.gu_out + m * 2 * F + col0 + c * 16;
-#pragma unroll
-            for (int j = 0; j < 16; j += 2) {
-              *reinterpret_cast<uint32_t*>(dg + j) =
-                  pack_bf16x2(__uint_as_float(raw[j]) * p.alpha, __uint_as_float(raw[j + 1]) * p.alpha);
-              *reinterpret_cast<uint32_t*>(dg + F + j) =
-                  pack_bf16x2(__uint_as_float(raw[16 + j]) * p.alpha, __uint_as_float(raw[16 + j + 1]) * p.alpha);
-            }
           }
         }
         tc_fence_before();
@@ -884,6 +874,21 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
         if (lane == 0) {                           // drained: the next tile's MMAs may start
           if (CG == 2 && rank != 0) mbar_arrive_cluster(acc_empty_l);
           else mbar_arrive(acc_empty);
+        }
+        if (p.gu_out && m < p.M) {                 // test-only output: the bf16 gate/up values the math used
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            __nv_bfloat16* dg = p.gu_out + m * 2 * F + col0 + 2 * i;
+            *reinterpret_cast<uint32_t*>(dg) = hp[i];
+            *reinterpret_cast<uint32_t*>(dg + F) = upk[i];
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const uint32_t gp = hp[i], up = upk[i];
+          const uint32_t sp = pack_bf16x2(silu_fast(__uint_as_float(gp << 16)), silu_fast(__uint_as_float(gp & 0xFFFF0000u)));
+          hp[i] = pack_bf16x2(__uint_as_float(sp << 16) * __uint_as_float(up << 16),
+                              __uint_as_float(sp & 0xFFFF0000u) * __uint_as_float(up & 0xFFFF0000u));
         }
         if (lane == 0) tma_store_wait_read();      // the staging box is free once the previous store read it
         __syncwarp();
