@@ -4,7 +4,7 @@
 
 One step = ``tfimage.linear.swiglu_mlp`` on one image's rows: quantize X [4352, 3072] under the gate/up input
 scale, gate/up NVFP4 GEMM [16384, 3072] whose epilogue applies SwiGLU and writes NVFP4 rows, down NVFP4 GEMM
-[3072, 8192] -> bf16 [4352, 3072]; 657.13 GFLOP. Inputs are resident in HBM; L2 is flushed (a 256 MiB write)
+[3072, 8192] -> bf16 [4352, 3072]; 657.13 GFLOP. Inputs are resident in HBM; L2 is flushed (a 256 MiB write, then a read of it)
 between steps, outside the per-step CUDA events. Under torchrun every rank runs its own image (independent seeds,
 no collective: weak scaling) and the result is whole-job TFLOP/s over the max per-rank time.
 
@@ -218,9 +218,18 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------------------------- configs[0], [2], [3] legs
+def l2_flush(buf) -> None:
+    """Evict L2 before a timed run: write a buffer larger than L2 (126 MB), then read it back, so the lines left in
+    L2 are clean -- after the write alone the timed kernel would first pay for writing ~126 MB of dirty flush data
+    back to HBM (it showed up as a 2x slower first kernel of every step)."""
+    buf.zero_()
+    buf.sum()
+
+
 def config_legs(dev, fp4_peak: float, fp8_peak: float, hbm_gbs: float) -> dict:
     """The other BASELINE configs measured beside the headline: each kernel timed alone with CUDA events on the
-    launching stream, L2 flushed (256 MiB write) before every iteration, median of 20 after 3 warm-up runs."""
+    launching stream, L2 flushed (256 MiB write, then a read of it) before every iteration, median of 20 after 3
+    warm-up runs."""
     import numpy as np
     import torch
 
@@ -237,7 +246,7 @@ def config_legs(dev, fp4_peak: float, fp8_peak: float, hbm_gbs: float) -> dict:
             fn()
         ts = []
         for _ in range(it):
-            flush.zero_()
+            l2_flush(flush)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
             fn()
@@ -497,13 +506,13 @@ def run_ours(args):
 
     for _ in range(args.warmup):
         step([torch.cuda.Event(enable_timing=True) for _ in range(4)])
-        flush.zero_()
+        l2_flush(flush)
     events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     barrier()
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             step(events[i])
-            flush.zero_()
+            l2_flush(flush)
         barrier()
     per = [[e[j].elapsed_time(e[j + 1]) for j in range(3)] for e in events]      # ms: quant, gate/up, down
     step_ms = [sum(p) for p in per]
@@ -522,7 +531,7 @@ def run_ours(args):
         L.swiglu_mlp_host(gate_up, down, x_host, y_host, chunks=M_ROWS // 256, graph=True)
     barrier()
     for a, b in e2e_ev:
-        flush.zero_()
+        l2_flush(flush)
         a.record(stream)
         L.swiglu_mlp_host(gate_up, down, x_host, y_host, chunks=M_ROWS // 256, graph=True)
         b.record(stream)
@@ -568,7 +577,7 @@ def run_ours(args):
             "vs_baseline": None, "dtype": "nvfp4", "data": "synthetic",
             "config": {"workload": WORKLOAD, "M": M_ROWS, "K": K_DIM, "F": F_DIM, "global_batch": world,
                        "rows_per_gpu": M_ROWS, "parallelism": f"dp{world} (independent images, no collective)",
-                       "l2": "flushed between steps: 256 MiB write outside the per-step events"},
+                       "l2": "flushed between steps: 256 MiB write then read back (clean lines) outside the per-step events"},
             "pct_fp4_peak": value / world / fp4_peak, "pct_fp4_nominal": value / world / 9000.0,
             "kernels_ms": {"quant_x": q_ms, "gate_up_swiglu_nvfp4": gu_ms, "down": down_ms},
             "roofline": {"bound": "tensor", "kernel": "gemm_kernel<MODE_FP4_SWIGLU> (gate/up + SwiGLU->NVFP4)",
