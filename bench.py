@@ -34,36 +34,14 @@ M_ROWS, K_DIM, F_DIM = 4352, 3072, 8192
 FLOP_GU = 2 * M_ROWS * K_DIM * 2 * F_DIM          # 438.09 GFLOP
 FLOP_DOWN = 2 * M_ROWS * F_DIM * K_DIM            # 219.04 GFLOP
 FLOP_STEP = FLOP_GU + FLOP_DOWN
-FP4_TO_BF16 = 4.0                                  # B200 dense FP4 : BF16 tensor rate (9 : 2.25 PFLOP/s)
-# DRAM bytes per gate/up launch (dram__bytes_read.sum + dram__bytes_write.sum) from the ncu capture summarised in
-# profiles/gemm_nvfp4_config1.md.
+# Nominal dense tensor peaks of one B200 (MEASURED_PEAKS.json carries HBM and bf16 figures only, so the FP4 / FP8
+# fractions are against these nominal numbers).
+FP4_NOMINAL_TFLOPS, FP8_NOMINAL_TFLOPS = 9000.0, 4500.0
+# DRAM bytes per gate/up launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of this launch
+# (1.03 x its 35.8 MB of algorithmic operand bytes).
 TRAFFIC_GU = 36.87e6
 WORKLOAD = ("configs[1] fused NVFP4 MLP pair: X bf16 [4352,3072] N(0,1) -> gate/up W [16384,3072] N(0,0.02) with "
             "SwiGLU->NVFP4 epilogue -> down W [3072,8192] N(0,0.02) -> bf16 [4352,3072]")
-
-
-def issue_peaks():
-    """Dense FP4 and FP8 MMA ceilings measured live by csrc/mma_peak_probe.cu (built by build.py --probe):
-    {"fp4": (TFLOP/s, cycles per MMA), "fp8": (...)}; missing entries when the probe is absent."""
-    import re
-    import subprocess
-    exe = ROOT / "qwen-image21-tensorfold-rtx_b200" / "_build" / "mma_peak_probe"
-    if not exe.exists():
-        return {}
-    try:
-        out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60).stdout
-    except (OSError, subprocess.SubprocessError):
-        return {}
-    found = {}
-    for key, pat in (("fp4", r"mxf4nvf4"), ("fp8", r"f8f6f4")):
-        m = re.search(pat + r".*?([0-9.]+) cycles/MMA\s+([0-9.]+) TFLOP/s", out)
-        if m:
-            found[key] = (float(m.group(2)), float(m.group(1)))
-    return found
-
-
-def fp4_issue_peak():
-    return issue_peaks().get("fp4")
 
 
 def peaks():
@@ -81,7 +59,8 @@ REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_c
 
 
 class ClockSampler:
-    """NVML SM clock + throttle reasons sampled every ~5 ms on a background thread."""
+    """NVML SM clock + throttle reasons on a background thread: one sample when the region opens, one every ~1 ms,
+    one when it closes (a timed region of a few ms still gets several)."""
 
     def __init__(self, index: int):
         self.index, self.samples, self.reasons, self.max_mhz = index, [], 0, None
@@ -96,17 +75,21 @@ class ClockSampler:
         except Exception:                                   # noqa: BLE001 -- no NVML: report no clocks
             self.nv = None
 
+    def _sample(self):
+        try:
+            self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:                                   # noqa: BLE001
+            pass
+
     def _run(self):
         while not self._stop.is_set():
-            try:
-                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
-                self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-            except Exception:                               # noqa: BLE001
-                pass
-            time.sleep(0.005)
+            self._sample()
+            time.sleep(0.001)
 
     def __enter__(self):
         if self.nv is not None:
+            self._sample()
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
         return self
@@ -115,6 +98,7 @@ class ClockSampler:
         self._stop.set()
         if self._t:
             self._t.join()
+            self._sample()
 
     def report(self):
         if not self.samples:
@@ -182,6 +166,91 @@ def cpu_baseline(budget_s: float = 10.0, rows: int = 64):
             "sample": f"{rows} of the {M_ROWS} rows per step, {n} steps over {budget_s:.0f} s: oracle NVFP4 "
                       f"quantize+dequantize, torch fp32 matmul, SwiGLU, requantize, fp32 matmul (weights "
                       f"dequantized once outside the timing)"}
+
+
+def cpu_baseline_fusions(budget_s: float = 4.0, rows: int = 256) -> dict:
+    """configs[2] on the host cores: the reference's fusions as restated in oracle/ (AdaLN + shift -> bf16 -> NVFP4
+    codes + scales; RMSNorm + RoPE of q and k from a qkv row block), on ``rows`` rows per call, reported as GB/s of
+    the same algorithmic bytes per row as the GPU legs."""
+    import numpy as np
+    import torch
+
+    from oracle import fusions as ofu
+    from oracle import nvfp4 as onv
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(23)
+    D, H, Dh = 3072, 24, 128
+    x = onv.bf16_round(rng.standard_normal((1, rows, D)).astype(np.float32))
+    sc = (rng.standard_normal((1, 1, D)) * 0.1).astype(np.float32)
+    sh = (rng.standard_normal((1, 1, D)) * 0.1).astype(np.float32)
+    qkv = onv.bf16_round(rng.standard_normal((1, rows, 3, H, Dh)).astype(np.float32))
+    w = (rng.standard_normal(Dh) * 0.05 + 1).astype(np.float32)
+    ang = rng.uniform(0, 6.3, (rows, Dh // 2)).astype(np.float32)
+    cos, sin = np.cos(ang), np.sin(ang)
+
+    def run(fn):
+        fn()
+        n, t0 = 0, time.perf_counter()
+        while n == 0 or time.perf_counter() - t0 < budget_s / 2:
+            fn()
+            n += 1
+        return (time.perf_counter() - t0) / n
+
+    t_ada = run(lambda: onv.quantize(ofu.adaln(x, sc, 1e-6, shift=sh).reshape(rows, D), 0.004))
+    t_rope = run(lambda: (ofu.rms_rope(qkv, 0, w, cos, sin, 1e-6), ofu.rms_rope(qkv, 1, w, cos, sin, 1e-6)))
+    ada_bytes = rows * (D * 2 + D // 2 + D // 16)
+    rope_bytes = rows * (4 * H * Dh * 2 + 2 * 64 * 8)
+    return {"adaln_quant_gbs": ada_bytes / t_ada / 1e9, "rms_rope_q_k_gbs": rope_bytes / t_rope / 1e9,
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{rows} rows per call (numpy restatement of kernels.py:14-70 + the NVFP4 quantizer)"}
+
+
+def _sdpa_cpu(q, k, v, causal=False):
+    """The reference's attention op (torch SDPA) on the host cores in fp32, for the CPU block timing."""
+    import numpy as np
+    import torch
+    import torch.nn.functional as F
+
+    from oracle import nvfp4 as onv
+
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).transpose(1, 2)   # noqa: E731
+    o = F.scaled_dot_product_attention(t(q), t(k), t(v), is_causal=causal)
+    return onv.bf16_round(o.transpose(1, 2).contiguous().numpy())
+
+
+def cpu_baseline_dit(model, prefix, layers: int) -> dict:
+    """configs[4] on the host cores: one image block of the step at full size (4096 image rows attending to the
+    256-row kept prefix), the reference's CPU arithmetic as restated in oracle/dit.py (NVFP4 quantize -> dequantize
+    -> fp32 matmul per linear, fusions, torch SDPA in fp32), with the model's own NVFP4 weights; the step estimate
+    is that block's time x the number of blocks (every image block has the same shapes)."""
+    import numpy as np
+    import torch
+
+    from oracle import dit as odit
+    from tfimage import mmdit
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg, dev = model.cfg, model.device
+    b = model.img_blocks[0]
+    N = 64 * 64
+    g = torch.Generator().manual_seed(41)
+    x = torch.randn((1, N, cfg.dim), generator=g).to(torch.bfloat16).float().numpy()
+    mod = [t.reshape(1, -1).float().cpu().numpy()
+           for t in model._mod(model._temb(torch.tensor([0.5], device=dev)), model.mod_img)]
+    cos, sin = mmdit.rope_table(mmdit.image_ids(64, 64, prefix.next_pos, dev), cfg)
+    cos, sin = cos.cpu().numpy(), sin.cpu().numpy()
+    kp, vp = (t.float().cpu().numpy() for t in prefix.kv[0])
+    lin = {n: (getattr(b, n).lin.codes.cpu().numpy(), getattr(b, n).lin.scales().view(torch.uint8).cpu().numpy(),
+               getattr(b, n).lin.scale, getattr(b, n).lin.act) for n in ("qkv", "out", "gate_up", "down")}
+    nq, nk = b.norm_q.cpu().numpy(), b.norm_k.cpu().numpy()
+    t0 = time.perf_counter()
+    y = odit.block(x, mod, cos, sin, kp, vp, lin, nq, nk, cfg.heads, cfg.eps, attn=_sdpa_cpu)
+    block_s = time.perf_counter() - t0
+    return {"block_s": block_s, "step_s_estimate": block_s * layers, "img_per_s_estimate": 1.0 / (block_s * layers * 25),
+            "cores": torch.get_num_threads(), "kind": "port", "finite": bool(np.isfinite(y).all()),
+            "sample": f"one image block timed once ({N} rows + {prefix.length}-row prefix, weight dequantization "
+                      f"included); step = {layers} x block, img/s = 1 / (25 steps x step)"}
 
 
 def run_reference(args):
@@ -357,9 +426,10 @@ DIT_WORKLOAD = ("configs[4] synthetic double-stream MMDiT, NVFP4: 28 blocks, hid
                 "N(0, 1), K/V prefix-cached once per prompt; 25 Euler steps; 32 seeds split across ranks")
 
 
-def dit_leg(world: int, rank: int, dev, barrier, reduce_max) -> dict:
+def dit_leg(world: int, rank: int, dev, barrier, reduce_max):
     """single-image DiT step latency at 4096 tokens, and images/s of the 25-step sampler over 32 seeds
-    split across the ranks (each rank a full weight replica, no collective on the data path)."""
+    split across the ranks (each rank a full weight replica, no collective on the data path). Returns the numbers
+    and (model, prefix, layers) for the CPU block timing."""
     import torch
 
     from tfimage import mmdit
@@ -437,7 +507,7 @@ def dit_leg(world: int, rank: int, dev, barrier, reduce_max) -> dict:
         barrier()
     sample_s = reduce_max(a.elapsed_time(b)) / 1e3
     ok = bool(torch.isfinite(lat_out).all())
-    return {"workload": DIT_WORKLOAD, "step_ms_at_4096_tokens": step_ms, "step_ms_eager": step_ms_eager,
+    info = {"workload": DIT_WORKLOAD, "step_ms_at_4096_tokens": step_ms, "step_ms_eager": step_ms_eager,
             "step_batch": 1,
             "img_per_s": DIT_SEEDS / sample_s, "sample_s": sample_s, "seeds": DIT_SEEDS,
             "seeds_per_rank": counts, "steps": DIT_STEPS, "scaling": "strong (32 seeds split across ranks)",
@@ -451,6 +521,106 @@ def dit_leg(world: int, rank: int, dev, barrier, reduce_max) -> dict:
                       "warm-up, each step one replayed CUDA graph of the forward (eager launches: step_ms_eager); "
                       "throughput = one timed 25-step sampler run (graph steps, prefix pass included) after a "
                       "warm-up step"}
+    return info, (model, prefix, model.cfg.layers)
+
+
+# ------------------------------------------------------------------------------------------------- summary
+def summary(line: dict) -> dict:
+    """The numbers of every BASELINE config in a few short keys, printed last in the line (a reader that keeps only
+    the line's tail still sees them): configs[0] GEMM, configs[2] fusions, configs[3] FP8 GEMMs, configs[4] DiT
+    step / images per second / tensor-parallel step, the CPU arms and the host link."""
+    def r(v, n=3):
+        return None if v is None else round(float(v), n)
+
+    out = {"c1_mlp_tflops": r(line["value"], 1), "c1_gu_frac_fp4": r(line["roofline"]["frac"]),
+           "c1_e2e_tflops": r(line["e2e"]["value"], 1)}
+    cf = line.get("configs")
+    if cf:
+        c0, c2, c3 = cf["configs[0]"], cf["configs[2]"], cf["configs[3]"]
+        out.update(c0_gemm_us=r(c0["gemm_us"], 2), c0_gemm_tflops=r(c0["gemm_tflops"], 1),
+                   c0_frac_fp4=r(c0["gemm_frac_fp4_peak"]), c0_quant_us=r(c0["quant_us"], 2),
+                   c0_linear_tflops=r(c0["linear_tflops"], 1),
+                   c2_adaln_quant_gbs=r(c2["adaln_quant_gbs"], 0), c2_adaln_quant_frac=r(c2["adaln_quant_frac_hbm"]),
+                   c2_rope_qkv_gbs=r(c2["rms_rope_qkv_gbs"], 0), c2_rope_qkv_frac=r(c2["rms_rope_qkv_frac_hbm"]),
+                   c3_fp8_tflops=[r(c3[k]["tflops"], 0) for k in ("linear_3072", "gate_up_16384", "down_3072_k8192")],
+                   c3_frac_fp8=[r(c3[k]["frac_fp8_peak"]) for k in ("linear_3072", "gate_up_16384", "down_3072_k8192")])
+    d = line.get("dit")
+    if d:
+        out.update(c4_step_ms=r(d["step_ms_at_4096_tokens"]), c4_img_per_s=r(d["img_per_s"]),
+                   c4_img_per_s_per_gpu=r(d["img_per_s"] / line["n_gpus"]))
+        tp = d.get("tensor_parallel_latency")
+        if tp:
+            out.update(c4_tp_world=tp["world"], c4_tp_step_ms_fused=r(tp["step_ms"]),
+                       c4_tp_step_ms_nccl=r(tp["step_ms_nccl"]))
+    cb = line.get("cpu_baseline")
+    if cb:
+        out["cpu_c1_tflops"] = r(cb["value"], 4)
+    if line.get("cpu_baseline_configs2"):
+        out["cpu_c2_adaln_quant_gbs"] = r(line["cpu_baseline_configs2"]["adaln_quant_gbs"])
+    if line.get("cpu_baseline_configs4"):
+        out["cpu_c4_step_s"] = r(line["cpu_baseline_configs4"]["step_s_estimate"], 1)
+    hl = line["e2e"].get("host_link", {})
+    out.update(link_h2d_gbs=r(hl.get("h2d_gbs_per_rank"), 1), link_both_gbs=r(hl.get("both_gbs_per_rank"), 1))
+    out["device_status"] = line.get("device_status")
+    return out
+
+
+# --------------------------------------------------------------------------------------------- profile legs
+PROFILE_LEGS = ("gemm0", "fp8_3072", "adaln_quant", "swiglu")
+
+
+def run_profile_leg(name: str, reps: int = 4) -> None:
+    """One kernel of one BASELINE config, launched ``reps`` times on cuda:0 with only its own operands allocated
+    (a few hundred MB at most), for ncu captures of a single launch:
+      gemm0        configs[0] NVFP4 GEMM   X codes [4096, 3072] x W [3072, 3072]
+      fp8_3072     configs[3] FP8 GEMM     X e4m3 [4968, 3072] x W [3072, 3072], per-channel W scales
+      adaln_quant  configs[2] AdaLN + shift + NVFP4 quantize on x [4352, 3072]
+      swiglu       configs[1] gate/up NVFP4 GEMM with the SwiGLU -> NVFP4 epilogue (M 4352, F 8192, K 3072)
+    Prints one line per launch with its CUDA-event time (for orientation only; never a bench value)."""
+    import torch
+
+    from tfimage import _lib
+    from tfimage import kernels as Kn
+    from tfimage import linear as L
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator().manual_seed(77)
+    if name == "gemm0":
+        x = torch.randn(4096, 3072, generator=g).to(torch.bfloat16).to(dev)
+        lin = L.Nvfp4Linear((torch.randn(3072, 3072, generator=g) * 0.02).to(torch.bfloat16).to(dev))
+        lin.set_act(float(_lib.absmax(x)) / (6 * 448))
+        q = lin.quantize(x)
+        fn = lambda: lin(q)                                                    # noqa: E731
+    elif name == "fp8_3072":
+        x = torch.randn(4968, 3072, generator=g).to(torch.bfloat16).to(dev)
+        f8 = L.Fp8Linear((torch.randn(3072, 3072, generator=g) * 0.02).to(torch.bfloat16).to(dev), per_channel=True)
+        a = _lib.fp8_act_scale(x)
+        q8 = _lib.quant_fp8(x, a)
+        fn = lambda: _lib.gemm_fp8(q8, f8.w8.view(torch.uint8), 4968, 3072, 3072, a, f8.ws)   # noqa: E731
+    elif name == "adaln_quant":
+        x = torch.randn(1, 4352, 3072, generator=g).to(torch.bfloat16).to(dev)
+        sc = (torch.randn(1, 1, 3072, generator=g) * 0.1).to(dev)
+        sh = (torch.randn(1, 1, 3072, generator=g) * 0.1).to(dev)
+        fn = lambda: Kn.adaln(x, sc, 1e-6, shift=sh, quant=0.004)               # noqa: E731
+    elif name == "swiglu":
+        x = torch.randn(4352, 3072, generator=g).to(torch.bfloat16).to(dev)
+        gu = L.Nvfp4Linear((torch.randn(2 * 8192, 3072, generator=g) * 0.02).to(torch.bfloat16).to(dev))
+        gu.set_act(float(_lib.absmax(x)) / (6 * 448))
+        q = gu.quantize(x)
+        fn = lambda: _lib.gemm_nvfp4_swiglu(q.codes, q.sf, gu.lin.codes, gu.lin.bs, 4352, 8192, 3072,  # noqa: E731
+                                             q.act * gu.lin.scale, 0.004)
+    else:
+        raise SystemExit(f"unknown profile leg {name!r}; one of {PROFILE_LEGS}")
+    stream = torch.cuda.current_stream(dev)
+    for i in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        print(f"{name} launch {i}: {a.elapsed_time(b) * 1e3:.1f} us", flush=True)
+    assert _lib.device_status() == 0
 
 
 # ------------------------------------------------------------------------------------------------------ our arm
@@ -548,29 +718,48 @@ def run_ours(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t[0])
 
-    dit = None
+    # the host link alone, per rank (every rank at once, max over ranks): the step's 26.7 MB in, out, and both at
+    # once on two streams -- what bounds e2e when the copies of all ranks share the host's memory and PCIe
+    link = {}
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    y_dev = torch.empty((M_ROWS, K_DIM), dtype=torch.bfloat16, device=dev)
+    for name, ops in (("h2d", (("in",),)), ("d2h", (("out",),)), ("both", (("in",), ("out",)))):
+        evs = []
+        for _ in range(5):
+            barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for (kind,) in ops:
+                st_ = s_in if kind == "in" else s_out
+                st_.wait_stream(stream)
+                with torch.cuda.stream(st_):
+                    if kind == "in":
+                        x.copy_(x_host, non_blocking=True)
+                    else:
+                        y_host.copy_(y_dev, non_blocking=True)
+                stream.wait_stream(st_)
+            b.record(stream)
+            evs.append((a, b))
+        barrier()
+        ms = reduce_max(statistics.median(a.elapsed_time(b) for a, b in evs))
+        nbytes = x_host.numel() * 2 * len(ops)
+        link[name + "_gbs_per_rank"] = nbytes / (ms * 1e-3) / 1e9
+    del y_dev
+
+    dit, dit_model = None, None
     if not args.no_dit:
         del flush
-        dit = dit_leg(world, rank, dev, barrier, reduce_max)
+        dit, dit_model = dit_leg(world, rank, dev, barrier, reduce_max)
     status = _lib.device_status()
 
     if rank == 0:
         pk, src = peaks()
-        derived = FP4_TO_BF16 * pk["bf16_tflops"]
-        probes = issue_peaks()
-        probe = probes.get("fp4")
-        if probe:
-            fp4_peak = probe[0]
-            peak_note = (f"measured: tcgen05 mxf4nvf4 M128xN256xK64 issue-rate probe, {probe[1]:.1f} cycles/MMA, "
-                         f"{probe[0]:.0f} TFLOP/s (csrc/mma_peak_probe.cu); 4 x measured bf16 burst = {derived:.0f}; "
-                         f"nominal 9000")
-        else:
-            fp4_peak = derived
-            peak_note = f"4 x bf16 burst {pk['bf16_tflops']} TFLOP/s ({src}); nominal 9000"
+        fp4_peak = FP4_NOMINAL_TFLOPS
         gu_ms = statistics.median(p[1] for p in per)
         down_ms = statistics.median(p[2] for p in per)
         q_ms = statistics.median(p[0] for p in per)
         achieved = FLOP_GU / (gu_ms * 1e-3) / 1e12
+        e2e_ms = float(e2e_t[0])
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
@@ -578,26 +767,31 @@ def run_ours(args):
             "config": {"workload": WORKLOAD, "M": M_ROWS, "K": K_DIM, "F": F_DIM, "global_batch": world,
                        "rows_per_gpu": M_ROWS, "parallelism": f"dp{world} (independent images, no collective)",
                        "l2": "flushed between steps: 256 MiB write then read back (clean lines) outside the per-step events"},
-            "pct_fp4_peak": value / world / fp4_peak, "pct_fp4_nominal": value / world / 9000.0,
+            "pct_fp4_nominal": value / world / fp4_peak,
             "kernels_ms": {"quant_x": q_ms, "gate_up_swiglu_nvfp4": gu_ms, "down": down_ms},
             "roofline": {"bound": "tensor", "kernel": "gemm_kernel<MODE_FP4_SWIGLU> (gate/up + SwiGLU->NVFP4)",
                          "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s", "frac": achieved / fp4_peak,
                          "traffic": TRAFFIC_GU, "traffic_unit": "bytes per launch",
-                         "frac_of_nominal_9000": achieved / 9000.0, "peak_note": peak_note},
+                         "peak_note": "nominal dense FP4 of one B200 (MEASURED_PEAKS.json has no FP4 figure); "
+                                      f"4 x its measured bf16 burst = {4 * pk['bf16_tflops']:.0f} ({src})"},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": x_host.numel() * 2,
-                    "d2h_bytes_per_step": y_host.numel() * 2},
+                    "d2h_bytes_per_step": y_host.numel() * 2, "ms_per_step": e2e_ms,
+                    "copy_gbs_per_rank": (x_host.numel() + y_host.numel()) * 2 / (e2e_ms * 1e-3) / 1e9,
+                    "host_link": link},
             "gpu_launches": 3 * args.steps,
             "clocks": clk.report(),
             "device_status": status,
             "dit": dit,
         }
         if not args.no_configs:
-            fp8_peak = probes["fp8"][0] if "fp8" in probes else 2 * pk["bf16_tflops"]
-            line["configs"] = config_legs(dev, fp4_peak, fp8_peak, pk["hbm_gbs"])
-            line["configs"]["peaks"]["source"] = ("tcgen05 issue-rate probe (csrc/mma_peak_probe.cu); HBM: "
-                                                  f"MEASURED_PEAKS.json copy ({src})")
+            line["configs"] = config_legs(dev, fp4_peak, FP8_NOMINAL_TFLOPS, pk["hbm_gbs"])
+            line["configs"]["peaks"]["source"] = (f"FP4 / FP8: nominal dense; HBM: MEASURED_PEAKS.json copy ({src})")
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
+            line["cpu_baseline_configs2"] = cpu_baseline_fusions()
+            if dit_model is not None:
+                line["cpu_baseline_configs4"] = cpu_baseline_dit(*dit_model)
+        line["summary"] = summary(line)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -613,7 +807,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-dit", action="store_true", help="skip the configs[4] DiT leg (latency + img/s)")
     ap.add_argument("--no-configs", action="store_true", help="skip the configs[0], [2], [3] kernel lines")
+    ap.add_argument("--profile-leg", choices=PROFILE_LEGS, help="run one kernel of one config a few times (for ncu)")
     args = ap.parse_args()
+    if args.profile_leg:
+        run_profile_leg(args.profile_leg)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

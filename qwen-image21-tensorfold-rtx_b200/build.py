@@ -34,14 +34,6 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
-def build_probe() -> Path:
-    """The tcgen05 issue-rate roofline probe (csrc/mma_peak_probe.cu) -> _build/mma_peak_probe."""
-    OBJ.mkdir(exist_ok=True)
-    out = OBJ / "mma_peak_probe"
-    subprocess.run([nvcc(), *ARCH, "-O3", "-std=c++17", str(CSRC / "mma_peak_probe.cu"), "-o", str(out)], check=True)
-    return out
-
-
 def build(force: bool = False, verbose: bool = False) -> Path:
     OBJ.mkdir(exist_ok=True)
     headers = list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
@@ -67,9 +59,6 @@ if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
-    ap.add_argument("--probe", action="store_true", help="also build the tcgen05 issue-rate probe")
     a = ap.parse_args()
     print(build(a.force, a.verbose))
-    if a.probe:
-        print(build_probe())
     sys.exit(0)

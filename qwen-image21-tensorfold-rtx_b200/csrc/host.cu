@@ -4,6 +4,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "tfb_common.cuh"
@@ -30,21 +31,22 @@ tfb_status cuda_fail(cudaError_t e, const char* what) {
 namespace {
 constexpr int kMaxDevices = 64;
 DeviceInfo g_dev[kMaxDevices];
-bool g_dev_ok[kMaxDevices];
+// Set (release) after g_dev[dev] is filled; read (acquire) on the lock-free fast path.
+std::atomic<bool> g_dev_ok[kMaxDevices];
 std::mutex g_dev_mu;
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::atomic<PFN_cuTensorMapEncodeTiled_v12000> g_encode{nullptr};
 }  // namespace
 
 tfb_status device_info(const DeviceInfo** out) {
   int dev = 0;
   TFB_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return fail(TFB_BAD_ARG, "device ordinal %d out of range", dev);
-  if (g_dev_ok[dev]) {
+  if (g_dev_ok[dev].load(std::memory_order_acquire)) {
     *out = &g_dev[dev];
     return TFB_OK;
   }
   std::lock_guard<std::mutex> lock(g_dev_mu);
-  if (!g_dev_ok[dev]) {
+  if (!g_dev_ok[dev].load(std::memory_order_relaxed)) {
     int major = 0, minor = 0, sms = 0;
     TFB_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
     TFB_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
@@ -54,7 +56,7 @@ tfb_status device_info(const DeviceInfo** out) {
     void* p = nullptr;
     TFB_CUDA(cudaGetSymbolAddress(&p, g_err_word));
     g_dev[dev] = DeviceInfo{dev, sms, static_cast<int*>(p)};
-    g_dev_ok[dev] = true;
+    g_dev_ok[dev].store(true, std::memory_order_release);
   }
   *out = &g_dev[dev];
   return TFB_OK;
@@ -62,14 +64,17 @@ tfb_status device_info(const DeviceInfo** out) {
 
 tfb_status make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t rows,
                         uint64_t row_stride, uint32_t box_inner, uint32_t box_rows, bool swizzle) {
-  if (!g_encode) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = g_encode.load(std::memory_order_acquire);
+  if (!encode) {
     std::lock_guard<std::mutex> lock(g_dev_mu);
-    if (!g_encode) {
+    encode = g_encode.load(std::memory_order_relaxed);
+    if (!encode) {
       void* fn = nullptr;
       cudaDriverEntryPointQueryResult q;
       TFB_CUDA(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q));
       if (q != cudaDriverEntryPointSuccess || !fn) return fail(TFB_CUDA_ERR, "cuTensorMapEncodeTiled unavailable");
-      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+      g_encode.store(encode, std::memory_order_release);
     }
   }
   if (!aligned(base, 16) || row_stride % 16 != 0)
@@ -80,7 +85,7 @@ tfb_status make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint
   cuuint32_t box[2] = {box_inner, box_rows};
   cuuint32_t estr[2] = {1, 1};
   const CUtensorMapDataType dt = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -109,13 +114,15 @@ int64_t tfb_sf_tiled_bytes(int64_t rows, int64_t k) {
 tfb_status tfb_ipc_handle(const void* ptr, uint8_t* handle, int64_t* offset) {
   static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
   if (!ptr || !handle || !offset) return tfb::fail(TFB_BAD_ARG, "ipc_handle: null argument");
-  static PFN_cuMemGetAddressRange_v3020 range = nullptr;
-  if (!range) {
+  static std::atomic<PFN_cuMemGetAddressRange_v3020> s_range{nullptr};
+  PFN_cuMemGetAddressRange_v3020 range = s_range.load(std::memory_order_acquire);
+  if (!range) {   // two threads may both look it up; they store the same pointer
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
     TFB_CUDA(cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &fn, 12000, cudaEnableDefault, &q));
     if (q != cudaDriverEntryPointSuccess || !fn) return tfb::fail(TFB_CUDA_ERR, "cuMemGetAddressRange unavailable");
     range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+    s_range.store(range, std::memory_order_release);
   }
   CUdeviceptr base = 0;
   size_t size = 0;

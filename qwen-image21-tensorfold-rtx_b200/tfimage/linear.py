@@ -259,11 +259,15 @@ def gated_residual_(lin: Linear, x, res: torch.Tensor, gate: torch.Tensor) -> to
 
 
 def swiglu_mlp(gate_up: Linear, down: Linear, x: torch.Tensor, residual=None):
-    """linear.py:136-150: down(silu(gate) * up) in one pass when both are static-scale NVFP4: the gate/up GEMM's
-    epilogue writes the SwiGLU rows as NVFP4 under down's input scale, so no bf16 [M, 2F] or [M, F] tensor exists.
-    None if the layers cannot take it (the caller runs the unfused path). Needs F % 128 == 0 here (the reference:
-    F % 64). ``residual=(res, gate)`` (this build's addition): the down GEMM adds ``gate * y`` into ``res`` in place
-    (``res.addcmul_(y, gate)``) and ``res`` is returned."""
+    """linear.py:136-150, the fused MLP pair. Two libtfb launches after the input quantizer: the gate/up GEMM
+    computes both halves of each hidden column in one 256-wide tile, applies SwiGLU in its epilogue and quantizes
+    the result straight to NVFP4 codes + block scales under ``down``'s static input scale; the down GEMM consumes
+    those codes. The hidden activations never exist in bf16 in HBM.
+
+    Returns None (and the caller takes the unfused path, as with the reference) unless both layers are NVFP4 with
+    static input scales and ``down.k`` equals the hidden width F, a multiple of 64. ``residual=(res, gate)`` (this
+    build's addition): the down GEMM adds ``gate * y`` into ``res`` in place (``res.addcmul_(y, gate)``) and
+    ``res`` is returned."""
 
     if not (isinstance(gate_up, Nvfp4Linear) and isinstance(down, Nvfp4Linear)) or gate_up.dynamic or down.dynamic:
         return None

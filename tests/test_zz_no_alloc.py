@@ -12,7 +12,6 @@ from _helpers import bf16_cpu, f32, rel_l2
 from tfimage import _lib
 
 pytestmark = pytest.mark.gpu
-TOL_NVFP4 = 2e-3     # rel-L2 bound of the NVFP4 GEMM path
 
 
 def _case(dev, M, K, F, seed):
@@ -54,9 +53,11 @@ def test_static_scratch_mlp_matches_workspace_entry_point(dev, M, K, F):
     torch.cuda.synchronize()
     ref = f32(y_ws)
     assert torch.isfinite(y_ws.float()).all()
-    for y in outs:
-        assert torch.isfinite(y.float()).all()
-        assert rel_l2(f32(y), ref) <= TOL_NVFP4
+    for i, y in enumerate(outs):
+        # Same three kernels, same inputs, same stream: only the scratch location differs, so the outputs must be
+        # bit-identical (a scale block read from a neighbouring scratch region would show up here). The rel-L2 is
+        # reported only to size a failure.
+        assert torch.equal(y, y_ws), f"call {i}: differs from the workspace entry point (rel-L2 {rel_l2(f32(y), ref):.3e})"
 
 
 def test_static_scratch_rejects_oversized_calls(dev):
