@@ -44,17 +44,19 @@ def attention(q, k, v, causal: bool = False) -> np.ndarray:
 
 
 def block(x, mod, cos, sin, k_prefix, v_prefix, lin: dict, norm_q, norm_k, heads: int, eps: float,
-          causal: bool = False, return_parts: bool = False, attn=attention):
+          causal: bool = False, return_parts: bool = False, attn=attention, acc: str = "f32"):
     """x [B, N, dim] (bf16 values); mod = (shift1, scale1, gate1, shift2, scale2, gate2) each [B, dim];
     k_prefix / v_prefix [B, P, H, D] (P may be 0); lin[name] = (codes [n, k/2], row scales [n, k/16] (e4m3 bytes),
     weight global, input scale) for name in qkv, out, gate_up, down; ``attn(q, k, v, causal)`` -> bf16 values.
-    Returns the block output (and k, v and the two branch outputs)."""
+    Returns the block output (and, with ``return_parts``, its intermediates). ``acc``: the GEMMs' summation
+    ("f32" = the reference's fp32 matmul; "f64" = the exact sums, to measure how far another valid summation order
+    moves the block output)."""
     sh1, sc1, g1, sh2, sc2, g2 = [np.asarray(m, dtype=np.float32).reshape(x.shape[0], 1, -1) for m in mod]
     x = np.asarray(x, dtype=np.float32)
     B, N, Dm = x.shape
     a = fusions.adaln(x, sc1, eps, shift=sh1)
     wc, ws, wg, act = lin["qkv"]
-    qkv = nvfp4.linear(a.reshape(B * N, Dm), wc, ws, wg, act)
+    qkv = nvfp4.linear(a.reshape(B * N, Dm), wc, ws, wg, act, acc)
     Dh = qkv.shape[1] // (3 * heads)
     src = qkv.reshape(B, N, 3, heads, Dh)
     q = fusions.rms_rope(src, 0, norm_q, cos, sin, eps)
@@ -64,13 +66,13 @@ def block(x, mod, cos, sin, k_prefix, v_prefix, lin: dict, norm_q, norm_k, heads
     vv = np.concatenate([np.asarray(v_prefix, dtype=np.float32), v], axis=1)
     o = attn(q, kk, vv, causal)
     wc, ws, wg, act = lin["out"]
-    att = nvfp4.linear(o.reshape(B * N, heads * Dh), wc, ws, wg, act).reshape(B, N, Dm)
+    att = nvfp4.linear(o.reshape(B * N, heads * Dh), wc, ws, wg, act, acc).reshape(B, N, Dm)
     x = nvfp4.bf16_round(x + att * g1)
     m = fusions.adaln(x, sc2, eps, shift=sh2)
     gc, gs, gg, gact = lin["gate_up"]
     dc, ds, dg, dact = lin["down"]
-    y = mlp.forward(m.reshape(B * N, Dm), gc, gs, gg, dc, ds, dg, gact, dact).reshape(B, N, Dm)
+    y = mlp.forward(m.reshape(B * N, Dm), gc, gs, gg, dc, ds, dg, gact, dact, acc=acc).reshape(B, N, Dm)
     out = nvfp4.bf16_round(x + y * g2)
     if return_parts:
-        return out, dict(k=k, v=v, att=att, mlp=y)
+        return out, dict(a=a, qkv=qkv.reshape(B, N, -1), q=q, k=k, v=v, o=o, att=att, x1=x, m=m, mlp=y)
     return out

@@ -9,9 +9,12 @@ from __future__ import annotations
 
 import numpy as np
 
-from .nvfp4 import bf16_round, bf16_trunc
+from .nvfp4 import bf16_round, bf16_round_f64, bf16_trunc
 
 _ROUND = {"rne": bf16_round, "rz": bf16_trunc}
+# float64 results to bf16: one correct rounding ("rne"), or via fp32 then toward zero ("rz": Triton's CPU
+# interpreter computes in fp32 and truncates on a bf16 store)
+_ROUND64 = {"rne": bf16_round_f64, "rz": lambda y: bf16_trunc(np.asarray(y).astype(np.float32))}
 
 AXES = (16, 56, 56)
 THETA = 10000.0
@@ -32,7 +35,7 @@ def adaln(x, scale, eps: float, shift=None, rounding: str = "rne") -> np.ndarray
     y = xc / np.sqrt(var + eps) * (1.0 + s)
     if shift is not None:
         y = y + np.asarray(shift, dtype=np.float32).astype(np.float64).reshape(B, 1, D)
-    return _ROUND[rounding](y.astype(np.float32))
+    return _ROUND64[rounding](y)
 
 
 def rms_rope(src, part: int, w, cos, sin, eps: float, rounding: str = "rne") -> np.ndarray:
@@ -47,12 +50,22 @@ def rms_rope(src, part: int, w, cos, sin, eps: float, rounding: str = "rne") -> 
     c = np.asarray(cos, dtype=np.float32).astype(np.float64)[None, :, None, :]
     s = np.asarray(sin, dtype=np.float32).astype(np.float64)[None, :, None, :]
     out = np.stack([c * x0 - s * x1, s * x0 + c * x1], -1).reshape(x.shape)
-    return _ROUND[rounding](out.astype(np.float32))
+    return _ROUND64[rounding](out)
 
 
 def silu_bf16(g, rounding: str = "rne") -> np.ndarray:
-    g = np.asarray(g, dtype=np.float32)
-    return _ROUND[rounding]((g / (np.float32(1.0) + np.exp(-g))).astype(np.float32))
+    """bf16(silu(g)) of bf16 values g (kernels.py:80 rounds silu to bf16 before the product).
+
+    ``"rne"``: the correctly rounded bf16 of the exact silu (float64, one rounding) -- the value the standalone GPU
+    SwiGLU kernel of this build produces bit for bit, and one the reference's fp32 formula with an approximate exp
+    reaches within one bf16 ulp. ``"rz"``: the reference formula in fp32 (g / (1 + exp(-g))) truncated to bf16,
+    which is what the reference Triton kernel computes under the CPU interpreter (the golden fixture)."""
+    if rounding == "rz":
+        g = np.asarray(g, dtype=np.float32)
+        return bf16_trunc((g / (np.float32(1.0) + np.exp(-g))).astype(np.float32))
+    g = np.asarray(g, dtype=np.float64)
+    with np.errstate(over="ignore"):
+        return bf16_round_f64(g / (1.0 + np.exp(-g)))
 
 
 def swiglu(gu, rounding: str = "rne") -> np.ndarray:

@@ -19,19 +19,20 @@ import numpy as np
 from . import fusions, nvfp4
 
 
-def gate_up(x, gu_codes, gu_sf, g_gu: float, act_x: float) -> np.ndarray:
-    return nvfp4.linear(x, gu_codes, gu_sf, g_gu, act_x)
+def gate_up(x, gu_codes, gu_sf, g_gu: float, act_x: float, acc: str = "f32") -> np.ndarray:
+    return nvfp4.linear(x, gu_codes, gu_sf, g_gu, act_x, acc)
 
 
 def hidden(gu_bf16) -> np.ndarray:
     return fusions.swiglu(gu_bf16)
 
 
-def forward(x, gu_codes, gu_sf, g_gu, down_codes, down_sf, g_down, act_x, act_h, return_parts=False):
-    gu = gate_up(x, gu_codes, gu_sf, g_gu, act_x)
+def forward(x, gu_codes, gu_sf, g_gu, down_codes, down_sf, g_down, act_x, act_h, return_parts=False,
+            acc: str = "f32"):
+    gu = gate_up(x, gu_codes, gu_sf, g_gu, act_x, acc)
     h = hidden(gu)
     hc, hs = nvfp4.quantize(h, act_h)
-    y = nvfp4.bf16_round(nvfp4.gemm(hc, hs, act_h, down_codes, down_sf, g_down))
+    y = nvfp4.bf16_round(nvfp4.gemm(hc, hs, act_h, down_codes, down_sf, g_down, acc))
     if return_parts:
         return y, dict(gu=gu, h=h, h_codes=hc, h_sf=hs)
     return y

@@ -47,6 +47,19 @@ def bf16_round(x) -> np.ndarray:
     return r.astype(np.uint32).view(np.float32).reshape(np.shape(x))
 
 
+def bf16_round_f64(x) -> np.ndarray:
+    """float64 -> nearest bf16 (ties to even) with one rounding, as fp32 values. The value is first rounded to fp32
+    by round-to-odd (toward zero, last bit set if inexact); fp32 keeps 16 more significand bits than bf16, so the
+    round-to-nearest-even to bf16 that follows equals a single rounding of the float64 value (rounding to fp32 to
+    nearest first could land exactly on a bf16 midpoint and round a second time the wrong way)."""
+    x = np.asarray(x, dtype=np.float64)
+    f = x.astype(np.float32)
+    away = np.abs(f.astype(np.float64)) > np.abs(x)
+    f = np.where(away, np.nextafter(f, np.float32(0)), f).astype(np.float32)
+    inexact = (f.astype(np.float64) != x).astype(np.uint32)
+    return bf16_round((np.ascontiguousarray(f).view(np.uint32) | inexact).view(np.float32)).reshape(np.shape(x))
+
+
 def bf16_trunc(x) -> np.ndarray:
     """fp32 -> bf16 by rounding toward zero (what Triton's CPU interpreter does on a bf16 store)."""
     b = np.ascontiguousarray(np.asarray(x, dtype=np.float32)).view(np.uint32)
@@ -179,14 +192,21 @@ def sf_untile(tiled, R: int, K: int) -> np.ndarray:
 
 
 # ---------------------------------------------------------------------------------------------- reference GEMMs
-def gemm(a_codes, a_sf, ga: float, b_codes, b_sf, gb: float) -> np.ndarray:
-    """The reference's CPU path: dequantize both operands, fp32 matmul (tools/gemm_tf.py:43-44) -> fp32 [M, N]."""
+def gemm(a_codes, a_sf, ga: float, b_codes, b_sf, gb: float, acc: str = "f32") -> np.ndarray:
+    """The reference's CPU path: dequantize both operands, fp32 matmul (tools/gemm_tf.py:43-44) -> fp32 [M, N].
+
+    ``acc="f64"`` (a measuring aid, not the reference): the same products summed in float64, i.e. the exact result
+    up to float64 rounding -- the reference's fp32 result and any other fp32 summation order scatter around it."""
+    if acc == "f64":
+        A = dequantize(a_codes, a_sf, 1.0).astype(np.float64) * float(ga)
+        B = dequantize(b_codes, b_sf, 1.0).astype(np.float64) * float(gb)
+        return (A @ B.T).astype(np.float32)
     A = dequantize(a_codes, a_sf, ga)
     B = dequantize(b_codes, b_sf, gb)
     return A @ B.T
 
 
-def linear(x, b_codes, b_sf, gb: float, act: float) -> np.ndarray:
+def linear(x, b_codes, b_sf, gb: float, act: float, acc: str = "f32") -> np.ndarray:
     """Nvfp4Linear.__call__ (tfimage/linear.py:125-130): quantize x under ``act``, W4A4 GEMM, bf16 output."""
     ac, asf = quantize(x, act)
-    return bf16_round(gemm(ac, asf, act, b_codes, b_sf, gb))
+    return bf16_round(gemm(ac, asf, act, b_codes, b_sf, gb, acc))

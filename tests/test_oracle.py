@@ -243,3 +243,53 @@ def test_gguf_f16_output_and_bad_length():
     assert np.array_equal(ogguf.dequantize("Q4_K", raw, "f16"), y.astype(np.float16).astype(np.float32))
     with pytest.raises(ValueError):
         ogguf.dequantize("Q4_K", raw[:-1])
+
+
+def test_bf16_round_f64_is_a_single_correct_rounding():
+    # bf16 neighbours and their midpoint are exact in float64, so the correctly rounded result is decidable exactly
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal(20000) * np.exp2(rng.integers(-30, 30, 20000))
+    # values that double rounding gets wrong: a bf16 midpoint nudged by less than half an fp32 ulp
+    lo = nvfp4.bf16_round(rng.standard_normal(2000).astype(np.float32)).astype(np.float64)
+    mid = lo + np.abs(lo) * 2.0 ** -8
+    x = np.concatenate([x, mid + np.abs(mid) * 2.0 ** -30, mid - np.abs(mid) * 2.0 ** -30, mid])
+    got = nvfp4.bf16_round_f64(x).astype(np.float64)
+    # exact: the bf16 values on either side of x -- its float64 pattern truncated to 8 significand bits (toward
+    # zero), and that plus one bf16 step (away from zero) -- then the nearer one, ties to the even pattern
+    low = np.uint64((1 << 45) - 1)
+    bits = x.view(np.uint64)
+    down_bits = bits & ~low
+    down = down_bits.view(np.float64)
+    up = (down_bits + np.uint64(1 << 45)).view(np.float64)
+    even = ((down_bits >> np.uint64(45)) & np.uint64(1)) == 0
+    dd, du = np.abs(x - down), np.abs(up - x)          # exact: both neighbours are within 2^8 ulps of x
+    ref = np.where(dd < du, down, np.where(dd > du, up, np.where(even, down, up)))
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_silu_bf16_rne_is_correctly_rounded_and_near_the_reference_formula():
+    # (below g = -88.7 the fp32 formula's e^-g overflows and it returns -0, while the exact silu is still a normal
+    # bf16 down to g = -94; the comparison with the formula therefore stops at -85)
+    g = nvfp4.bf16_round(np.linspace(-85, 30, 200001).astype(np.float32))
+    exact = fusions.silu_bf16(g)                        # float64, one rounding
+    ref_fp32 = fusions.silu_bf16(g, rounding="rz")      # the reference formula in fp32 (truncated)
+    ulp = ulp_bf16(exact)
+    assert np.all(np.abs(exact - ref_fp32) <= ulp * 1.0001)
+    assert fusions.silu_bf16(np.float32(-90.0)) < 0     # -90 e^-90 = -7.4e-38: representable, not -0
+    # against an independent float64 evaluation with the single rounding
+    sel = np.abs(g) < 20
+    e64 = g[sel].astype(np.float64) / (1.0 + np.exp(-g[sel].astype(np.float64)))
+    np.testing.assert_array_equal(exact[sel], nvfp4.bf16_round_f64(e64))
+
+
+def test_gemm_oracle_exact_sums_option():
+    # float64 summation of the same products: equal to the fp32 result up to fp32 summation error
+    rng = np.random.default_rng(12)
+    x = nvfp4.bf16_round(rng.standard_normal((64, 512)).astype(np.float32))
+    w = nvfp4.bf16_round((rng.standard_normal((96, 512)) * 0.02).astype(np.float32))
+    gw = nvfp4.weight_global(np.abs(w).max())
+    wc, ws = nvfp4.quantize(w, gw)
+    ga = nvfp4.dynamic_act_global(np.abs(x).max())
+    xc, xs = nvfp4.quantize(x, ga)
+    a, b = nvfp4.gemm(xc, xs, ga, wc, ws, gw), nvfp4.gemm(xc, xs, ga, wc, ws, gw, acc="f64")
+    assert np.abs(a - b).max() <= 1e-5 * np.abs(b).max()
