@@ -485,9 +485,8 @@ def dit_leg(world: int, rank: int, dev, barrier, reduce_max):
             model.disable_tp()
             return ms
 
-        fused = world == 2                                   # the fused path is validated for 2 ranks
-        tp_lat = {"world": world, "step_ms": tp_step_ms(True, graph=True) if fused else None,
-                  "step_ms_eager": tp_step_ms(True) if fused else None, "step_ms_nccl": tp_step_ms(False),
+        tp_lat = {"world": world, "step_ms": tp_step_ms(True, graph=True), "step_ms_eager": tp_step_ms(True),
+                  "step_ms_nccl": tp_step_ms(False),
                   "split": "MLP: gate/up columns (pairs kept local) and down rows over the ranks; attention, qkv, "
                            "out replicated",
                   "collective": "step_ms (one replayed CUDA graph per step; step_ms_eager: launched eagerly): the reduction fused into the down GEMM (tfb_gemm_nvfp4_tp: partial tiles "
@@ -614,12 +613,12 @@ def run_profile_leg(name: str, reps: int = 4) -> None:
         raise SystemExit(f"unknown profile leg {name!r}; one of {PROFILE_LEGS}")
     stream = torch.cuda.current_stream(dev)
     for i in range(reps):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
         fn()
-        b.record(stream)
+        e1.record(stream)
         torch.cuda.synchronize(dev)
-        print(f"{name} launch {i}: {a.elapsed_time(b) * 1e3:.1f} us", flush=True)
+        print(f"{name} launch {i}: {e0.elapsed_time(e1) * 1e3:.1f} us", flush=True)
     assert _lib.device_status() == 0
 
 

@@ -81,8 +81,8 @@ tfb_status tfb_gemm_nvfp4(const uint8_t* a_codes, const uint8_t* a_sf, const uin
 
 /* W8A8 FP8 GEMM on tcgen05 kind::f8f6f4: y[M, N] = bf16(sum_k a[m,k] b[n,k] * a_scale * b_scale[n or 0]).
  * Scales are device fp32 (a_scale: one value; b_scale: N values if b_per_channel else one). Replaces
- * torch._scaled_mm in Fp8Linear.__call__ (tfimage/linear.py:98); M is ragged (no padding). K % 128 == 0,
- * N % 32 == 0. */
+ * torch._scaled_mm in Fp8Linear.__call__ (tfimage/linear.py:98); M is ragged (no padding). K % 16 == 0,
+ * N % 16 == 0 (the reference's FP8 envelope, tfimage/linear.py:159), ldy % 8 == 0. */
 tfb_status tfb_gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, int64_t K, const float* a_scale,
                         const float* b_scale, int b_per_channel, void* y, int64_t ldy, void* stream);
 
@@ -180,7 +180,8 @@ tfb_status tfb_rms_rope_qkv(const void* src, int64_t B, int64_t N, int64_t H, in
                             float eps, void* q, int64_t q_sb, int64_t q_sn, void* k, int64_t k_sb, int64_t k_sn,
                             void* v, int64_t v_sb, int64_t v_sn, void* stream);
 
-/* Standalone SwiGLU: gu bf16 [M, 2F] = [gate | up] -> out bf16 [M, F] = bf16(bf16(silu(gate)) * up).
+/* Standalone SwiGLU: gu bf16 [M, 2F] = [gate | up] -> out bf16 [M, F] = bf16(bf16(silu(gate)) * up), silu rounded
+ * correctly to bf16 (the round-to-nearest-even bf16 of the exact value).
  * Replaces the Triton _swiglu_kernel (tfimage/kernels.py:73-92). F % 8 == 0. */
 tfb_status tfb_swiglu(const void* gu, int64_t M, int64_t F, void* out, void* stream);
 

@@ -1,5 +1,8 @@
 // Fused elementwise kernels of a DiT block: AdaLN modulate (+ NVFP4 quantize), RMSNorm + RoPE, SwiGLU.
 // All are HBM-bound: 16-byte coalesced loads/stores, statistics in fp32 registers, one pass over the input.
+#include <algorithm>
+#include <atomic>
+
 #include "tfb_common.cuh"
 
 namespace tfb {
@@ -9,8 +12,14 @@ namespace {
 // WPR warps share a row (D = 256 * NCH): warp w of the row, lane l holds columns (i * WPR + w) * 256 + l * 8 .. +7
 // for its CPT = NCH / WPR chunks i, so every warp load / store covers 512 contiguous bytes and a 16-element
 // quantization block is the lane pair (2q, 2q+1). Row statistics: warp shuffles, then the WPR partial sums through
-// shared memory. Splitting the row keeps a thread's values in few registers (24 floats at D = 3072): with one warp
-// per row (96 floats per lane) only 16 warps fitted on an SM and the kernel ran at a third of HBM bandwidth.
+// shared memory (two passes over the register-held row: mean, then the centred sum of squares).
+//
+// A block (RPB row slots of WPR warps) walks a contiguous range of rows of ONE batch element, so the modulation of
+// its columns -- (1 + scale) and shift -- is staged once per block in shared memory ([chunk][half][lane][4] floats:
+// each 16-byte read of a warp is contiguous, no bank conflicts) instead of being re-read and re-added per element;
+// the next row's x is loaded into registers before the current row is computed. The arithmetic runs on packed fp32
+// pairs (sm_100 FFMA2 / FADD2 / FMUL2) and the NVFP4 block maximum on packed bf16 pairs. The previous form (one row
+// per warp group, per-element scale / shift loads, scalar math) was issue-bound at ~27 instructions per element.
 constexpr int kAdaThreads = 256;
 
 template <int NCH>
@@ -20,127 +29,199 @@ struct AdaSplit {
   static constexpr int RPB = (kAdaThreads / 32) / WPR;                                     // rows per block
 };
 
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 bf16x2_to_f2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+
 template <int NCH>
-__global__ void __launch_bounds__(kAdaThreads) adaln_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
-                                                            int64_t rows_total, int64_t rows_per_b,
+__global__ void __launch_bounds__(kAdaThreads) adaln_kernel(const __nv_bfloat16* __restrict__ x, int64_t B,
+                                                            int64_t N, int64_t rows_total, int chunks_per_b,
                                                             const float* __restrict__ scale,
                                                             const float* __restrict__ shift, float eps,
                                                             __nv_bfloat16* __restrict__ out, float qg,
                                                             uint8_t* __restrict__ codes, uint8_t* __restrict__ sf) {
-  pdl_trigger();
-  pdl_wait();
   using S = AdaSplit<NCH>;
   constexpr int D = NCH * 256, WPR = S::WPR, CPT = S::CPT, RPB = S::RPB;
+  extern __shared__ float4 ada_tab[];                      // [2][NCH][2][32] float4: (1 + scale), then shift
   __shared__ float red[2][RPB][WPR];
   // NVFP4 multiplier per scale byte, 1 / (e4m3(sf) * g) (0 for sf = 0): scales of non-negative amax are 0..0x7E,
   // so 128 entries cover them; one exact reciprocal per entry instead of one per 8 values
   __shared__ float inv_tab[128];
+  pdl_trigger();
+  pdl_wait();                                              // before any access to global memory
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int rib = warp / WPR, wr = warp % WPR;             // row inside the block, warp inside the row
-  if (codes && threadIdx.x < 128) inv_tab[threadIdx.x] = nvfp4_inv(threadIdx.x, nvfp4_enc(qg));
+  const int rib = warp / WPR, wr = warp % WPR;             // row slot inside the block, warp inside the row
   const bool warp_live = warp < RPB * WPR;                 // WPR = 3 leaves spare warps in the block
-  const int64_t row = blockIdx.x * (int64_t)RPB + rib;
-  const bool live = warp_live && row < rows;
-  float v[CPT][8];
-  float sum = 0.0f;
-  if (live) {
-    const __nv_bfloat16* xr = x + row * D;
+  if (codes && threadIdx.x < 128) inv_tab[threadIdx.x] = nvfp4_inv(threadIdx.x, nvfp4_enc(qg));
+  // this block's rows: chunk blockIdx.x of batch element blockIdx.y (y == B: the padding rows of the tiled scales)
+  const int64_t b = blockIdx.y;
+  const int64_t first = b < B ? b * N : B * N, count = b < B ? N : rows_total - B * N;
+  const int64_t per = (count + chunks_per_b - 1) / chunks_per_b;
+  const int64_t r0 = first + (int64_t)blockIdx.x * per, r1 = min(first + count, r0 + per);
+  const size_t sf_chunks = D >> 6;
+  if (b == B) {                                            // padding rows: zero scale words, nothing else
+    if (!warp_live) return;
+    for (int64_t row = r0 + rib; row < r1; row += RPB)
+      if ((lane & 7) == 0)
 #pragma unroll
-    for (int i = 0; i < CPT; ++i) {
-      unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(xr + (i * WPR + wr) * 256 + lane * 8)), v[i]);
+        for (int i = 0; i < CPT; ++i)
+          *reinterpret_cast<uint32_t*>(sf + sf_tiled_offset(row, (i * WPR + wr) * 16 + (lane >> 1), sf_chunks)) = 0u;
+    return;
+  }
+  const Nvfp4Enc enc = nvfp4_enc(qg);
+  uint4 nxt[CPT];
+  auto load_row = [&](int64_t row) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) sum += v[i][k];
+    for (int i = 0; i < CPT; ++i)
+      nxt[i] = row < r1 ? __ldg(reinterpret_cast<const uint4*>(x + row * D + (i * WPR + wr) * 256 + lane * 8))
+                        : make_uint4(0, 0, 0, 0);
+  };
+  int64_t row = r0 + rib;
+  if (warp_live) load_row(row);                            // the first row's loads go out before the table's
+  {
+    // 4 consecutive columns c..c+3 are one float4 of the [chunk][half][lane][4] layout; every load of the fill is
+    // in flight before the first store
+    constexpr int kV = (D / 4 + kAdaThreads - 1) / kAdaThreads;   // float4 per thread (the last may be past D)
+    float4 sv[kV], hv[kV];
+#pragma unroll
+    for (int k = 0; k < kV; ++k) {
+      const int c = (k * kAdaThreads + threadIdx.x) * 4;
+      const bool in = c < D;
+      sv[k] = in ? __ldg(reinterpret_cast<const float4*>(scale + b * D + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      hv[k] = in && shift ? __ldg(reinterpret_cast<const float4*>(shift + b * D + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int k = 0; k < kV; ++k) {
+      const int c = (k * kAdaThreads + threadIdx.x) * 4, ch = c >> 8, r = c & 255;
+      if (c >= D) continue;
+      const int q = ch * 64 + ((r >> 2) & 1) * 32 + (r >> 3);
+      ada_tab[q] = make_float4(1.0f + sv[k].x, 1.0f + sv[k].y, 1.0f + sv[k].z, 1.0f + sv[k].w);
+      ada_tab[NCH * 64 + q] = hv[k];
     }
   }
+  __syncthreads();                                         // the modulation table and inv_tab are in place
+  const int iters = (int)((r1 - r0 + RPB - 1) / RPB);
+  for (int it = 0; it < iters; ++it, row += RPB) {
+    const bool live = warp_live && row < r1;
+    float2 v[CPT][4];
 #pragma unroll
-  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  if (warp_live && lane == 0) red[0][rib][wr] = sum;
-  __syncthreads();
-  float mean = 0.0f;
-  if (warp_live) {
-#pragma unroll
-    for (int w = 0; w < WPR; ++w) mean += red[0][rib][w];
-    mean /= D;
-  }
-  float var = 0.0f;
-  if (live) {
+    for (int i = 0; i < CPT; ++i) {
+      v[i][0] = bf16x2_to_f2(nxt[i].x);
+      v[i][1] = bf16x2_to_f2(nxt[i].y);
+      v[i][2] = bf16x2_to_f2(nxt[i].z);
+      v[i][3] = bf16x2_to_f2(nxt[i].w);
+    }
+    if (warp_live) load_row(row + RPB);                   // the next row's loads are in flight during this row
+    float2 s2 = f2(0.0f, 0.0f);
 #pragma unroll
     for (int i = 0; i < CPT; ++i)
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        v[i][k] -= mean;
-        var += v[i][k] * v[i][k];
+      for (int k = 0; k < 4; ++k) s2 = __fadd2_rn(s2, v[i][k]);
+    float sum = s2.x + s2.y;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (warp_live && lane == 0) red[0][rib][wr] = sum;
+    __syncthreads();
+    float mean = 0.0f;
+#pragma unroll
+    for (int w = 0; w < WPR; ++w) mean += warp_live ? red[0][rib][w] : 0.0f;
+    mean /= D;
+    const float2 nm = f2(-mean, -mean);
+    float2 q2 = f2(0.0f, 0.0f);
+#pragma unroll
+    for (int i = 0; i < CPT; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        v[i][k] = __fadd2_rn(v[i][k], nm);
+        q2 = __ffma2_rn(v[i][k], v[i][k], q2);
       }
-  }
+    float var = q2.x + q2.y;
 #pragma unroll
-  for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
-  if (warp_live && lane == 0) red[1][rib][wr] = var;
-  __syncthreads();
-  if (!warp_live || row >= rows_total) return;
-  if (!live) {  // padding rows of the tiled scale layout: zero scales
-    if (sf && (lane & 7) == 0)
+    for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+    if (warp_live && lane == 0) red[1][rib][wr] = var;
+    __syncthreads();
+    if (live) {
+      float vs = 0.0f;
 #pragma unroll
-      for (int i = 0; i < CPT; ++i)
-        *reinterpret_cast<uint32_t*>(sf + sf_tiled_offset(row, (i * WPR + wr) * 16 + (lane >> 1), D >> 6)) = 0u;
-    return;
-  }
-  float vs = 0.0f;
+      for (int w = 0; w < WPR; ++w) vs += red[1][rib][w];
+      const float rstd = rsqrtf(vs / D + eps);
+      const float2 r2 = f2(rstd, rstd);
+      // this row's part of the tiled scale offset
+      const size_t sf_row = (static_cast<size_t>(row >> 7) * sf_chunks) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4;
 #pragma unroll
-  for (int w = 0; w < WPR; ++w) vs += red[1][rib][w];
-  const float rstd = rsqrtf(vs / D + eps);
-  const int64_t b = row / rows_per_b;
-  const float* sc = scale + b * D;
-  const float* sh = shift ? shift + b * D : nullptr;
-  const Nvfp4Enc enc = nvfp4_enc(qg);
-  // this row's part of the tiled scale offset; chunk ch's word for lanes 8t adds (4 ch + t) * 512
-  const size_t sf_row = sf ? (static_cast<size_t>(row >> 7) * (D >> 6)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4
-                           : 0;
-#pragma unroll
-  for (int i = 0; i < CPT; ++i) {
-    const int ch = i * WPR + wr;
-    const int c0 = ch * 256 + lane * 8;
-    const float4 s0 = __ldg(reinterpret_cast<const float4*>(sc + c0));
-    const float4 s1 = __ldg(reinterpret_cast<const float4*>(sc + c0 + 4));
-    float s8[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-    float y[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) y[k] = v[i][k] * rstd * (1.0f + s8[k]);
-    if (sh) {
-      const float4 h0 = __ldg(reinterpret_cast<const float4*>(sh + c0));
-      const float4 h1 = __ldg(reinterpret_cast<const float4*>(sh + c0 + 4));
-      const float h[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-#pragma unroll
-      for (int k = 0; k < 8; ++k) y[k] += h[k];
-    }
-    uint4 packed = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
-                              pack_bf16x2(y[6], y[7]));
-    if (out) *reinterpret_cast<uint4*>(out + row * D + c0) = packed;
-    if (codes) {
-      float q[8];
-      unpack_bf16x8(packed, q);  // quantize the bf16-rounded result
-      float amax = 0.0f;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(q[k]));
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-      const uint32_t sfb = nvfp4_scale(amax, enc);
-      *reinterpret_cast<uint32_t*>(codes + row * (D >> 1) + (c0 >> 1)) = nvfp4_codes8(q, inv_tab[sfb]);
-      // lanes 8t, 8t+2, 8t+4, 8t+6 hold blocks 4t..4t+3 of this chunk: one 32-bit word of the tiled layout
-      const uint32_t b1 = __shfl_down_sync(0xffffffffu, sfb, 2);
-      const uint32_t b2 = __shfl_down_sync(0xffffffffu, sfb, 4);
-      const uint32_t b3 = __shfl_down_sync(0xffffffffu, sfb, 6);
-      if ((lane & 7) == 0)
-        *reinterpret_cast<uint32_t*>(sf + sf_row + (size_t)(ch * 4 + (lane >> 3)) * 512) =
-            sfb | (b1 << 8) | (b2 << 16) | (b3 << 24);
+      for (int i = 0; i < CPT; ++i) {
+        const int ch = i * WPR + wr;
+        const int c0 = ch * 256 + lane * 8;
+        const float4 a0 = ada_tab[ch * 64 + lane], a1 = ada_tab[ch * 64 + 32 + lane];
+        const float4 h0 = ada_tab[NCH * 64 + ch * 64 + lane], h1 = ada_tab[NCH * 64 + ch * 64 + 32 + lane];
+        const float2 y0 = __ffma2_rn(__fmul2_rn(v[i][0], r2), f2(a0.x, a0.y), f2(h0.x, h0.y));
+        const float2 y1 = __ffma2_rn(__fmul2_rn(v[i][1], r2), f2(a0.z, a0.w), f2(h0.z, h0.w));
+        const float2 y2 = __ffma2_rn(__fmul2_rn(v[i][2], r2), f2(a1.x, a1.y), f2(h1.x, h1.y));
+        const float2 y3 = __ffma2_rn(__fmul2_rn(v[i][3], r2), f2(a1.z, a1.w), f2(h1.z, h1.w));
+        const uint4 packed = make_uint4(pack_bf16x2(y0.x, y0.y), pack_bf16x2(y1.x, y1.y), pack_bf16x2(y2.x, y2.y),
+                                        pack_bf16x2(y3.x, y3.y));
+        if (out) *reinterpret_cast<uint4*>(out + row * D + c0) = packed;
+        if (codes) {
+          // the bf16-rounded result is what gets quantized: block max on packed bf16 magnitudes, then the lane pair
+          const uint32_t ax = packed.x & 0x7FFF7FFFu, ay = packed.y & 0x7FFF7FFFu;
+          const uint32_t az = packed.z & 0x7FFF7FFFu, aw = packed.w & 0x7FFF7FFFu;
+          const __nv_bfloat162 mm = __hmax2(__hmax2(*reinterpret_cast<const __nv_bfloat162*>(&ax),
+                                                    *reinterpret_cast<const __nv_bfloat162*>(&ay)),
+                                            __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&az),
+                                                    *reinterpret_cast<const __nv_bfloat162*>(&aw)));
+          const uint32_t mw = *reinterpret_cast<const uint32_t*>(&mm);
+          float amax = fmaxf(__uint_as_float(mw << 16), __uint_as_float(mw & 0xFFFF0000u));
+          amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+          const uint32_t sfb = nvfp4_scale(amax, enc);
+          const float inv = inv_tab[sfb];
+          const float2 i2 = f2(inv, inv);
+          const float2 p0 = __fmul2_rn(bf16x2_to_f2(packed.x), i2), p1 = __fmul2_rn(bf16x2_to_f2(packed.y), i2);
+          const float2 p2 = __fmul2_rn(bf16x2_to_f2(packed.z), i2), p3 = __fmul2_rn(bf16x2_to_f2(packed.w), i2);
+          *reinterpret_cast<uint32_t*>(codes + row * (D >> 1) + (c0 >> 1)) =
+              e2m1x8(p0.x, p0.y, p1.x, p1.y, p2.x, p2.y, p3.x, p3.y);
+          // lane 2q holds block ch * 16 + q: byte (q % 4) of word ch * 4 + q / 4 of the row in the tiled layout
+          if ((lane & 1) == 0) sf[sf_row + (size_t)(ch * 4 + (lane >> 3)) * 512 + ((lane >> 1) & 3)] = (uint8_t)sfb;
+        }
+      }
     }
   }
 }
+
 template <int NCH>
-void launch_adaln(const void* x, int64_t rows, int64_t rows_total, int64_t rows_per_b, const float* scale,
-                  const float* shift, float eps, void* out, float qg, uint8_t* codes, uint8_t* sf, cudaStream_t s) {
+tfb_status launch_adaln(const DeviceInfo* di, const void* x, int64_t B, int64_t N, int64_t rows_total,
+                        const float* scale, const float* shift, float eps, void* out, float qg, uint8_t* codes,
+                        uint8_t* sf, cudaStream_t s) {
   constexpr int RPB = AdaSplit<NCH>::RPB;
-  const int64_t grid = (rows_total + RPB - 1) / RPB;
-  TFB_LAUNCH(adaln_kernel<NCH>, grid, kAdaThreads, s, static_cast<const __nv_bfloat16*>(x), rows, rows_total, rows_per_b,
-                                                 scale, shift, eps, static_cast<__nv_bfloat16*>(out), qg, codes, sf);
+  constexpr int kSmem = 2 * NCH * 256 * 4;                // (1 + scale) and shift, fp32
+  // blocks of this instantiation one SM holds at once, per device (set-up calls may race: they store the same value)
+  static std::atomic<int> resident[64];
+  int per_sm = resident[di->device].load(std::memory_order_acquire);
+  if (!per_sm) {
+    TFB_CUDA(cudaFuncSetAttribute(adaln_kernel<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    int n = 0;
+    TFB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, adaln_kernel<NCH>, kAdaThreads, kSmem));
+    per_sm = std::max(1, n);
+    resident[di->device].store(per_sm, std::memory_order_release);
+  }
+  // one resident wave of blocks over all batch elements, each walking at least RPB rows
+  const int64_t want = (int64_t)di->sm_count * per_sm;
+  const int64_t by_rows = (N + RPB - 1) / RPB;
+  const int chunks = (int)std::max<int64_t>(1, std::min<int64_t>(by_rows, (want + B - 1) / B));
+  const int pad_blocks = rows_total > B * N ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(chunks, (unsigned)(B + pad_blocks));
+  cfg.blockDim = dim3(kAdaThreads);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  TFB_CUDA(cudaLaunchKernelEx(&cfg, adaln_kernel<NCH>, static_cast<const __nv_bfloat16*>(x), B, N, rows_total,
+                              chunks, scale, shift, eps, static_cast<__nv_bfloat16*>(out), qg, codes, sf));
+  return TFB_OK;
 }
 
 // --------------------------------------------------------------------------------------------- RMSNorm + RoPE
@@ -230,8 +311,8 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __rest
   unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(gu + m * 2 * F + F + c)), u);
   float y[8];
 #pragma unroll
-  for (int k = 0; k < 8; k += 2) {   // silu rounded to bf16 two at a time (one paired conversion)
-    const uint32_t sp = pack_bf16x2(__fdiv_rn(g[k], 1.0f + expf(-g[k])), __fdiv_rn(g[k + 1], 1.0f + expf(-g[k + 1])));
+  for (int k = 0; k < 8; k += 2) {   // silu correctly rounded to bf16, two at a time (one paired conversion)
+    const uint32_t sp = pack_bf16x2(silu_for_bf16(g[k]), silu_for_bf16(g[k + 1]));
     y[k] = __uint_as_float(sp << 16) * u[k];
     y[k + 1] = __uint_as_float(sp & 0xFFFF0000u) * u[k + 1];
   }
@@ -262,15 +343,17 @@ tfb_status tfb_adaln(const void* x, int64_t B, int64_t N, int64_t D, const float
   const int64_t rows = B * N;
   const int64_t rows_total = codes ? (rows + 127) / 128 * 128 : rows;
   if (rows_total == 0) return TFB_OK;
+  if (B > 65535) return fail(TFB_BAD_SHAPE, "adaln: at most 65535 batch elements (B=%lld)", (long long)B);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (D / 256) {
 #define TFB_ADA(n) \
-  case n: launch_adaln<n>(x, rows, rows_total, N, scale, shift, eps, out, q_global, codes, sf, s); break;
+  case n: st = launch_adaln<n>(di, x, B, N, rows_total, scale, shift, eps, out, q_global, codes, sf, s); break;
     TFB_ADA(1) TFB_ADA(2) TFB_ADA(3) TFB_ADA(4) TFB_ADA(6) TFB_ADA(8) TFB_ADA(12) TFB_ADA(16) TFB_ADA(24) TFB_ADA(32)
 #undef TFB_ADA
     default:
       return fail(TFB_BAD_SHAPE, "adaln: D=%lld not instantiated (256 x {1,2,3,4,6,8,12,16,24,32})", (long long)D);
   }
+  if (st != TFB_OK) return st;
   TFB_CUDA(cudaGetLastError());
   return TFB_OK;
 }

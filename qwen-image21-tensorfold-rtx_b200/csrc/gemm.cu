@@ -377,8 +377,8 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
 __device__ __forceinline__ void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-// silu(g) = g / (1 + e^-g) with the hardware exp2 and reciprocal approximations (the reference's Triton kernel
-// used approximate math too); the result is rounded to bf16 by the caller.
+// silu(g) = g / (1 + e^-g) with the hardware exp2 and reciprocal approximations (used by the SwiGLU GEMM epilogue;
+// the caller rounds the result to bf16).
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 
@@ -853,6 +853,12 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
             *reinterpret_cast<uint32_t*>(dg + F) = upk[i];
           }
         }
+        // h = bf16(bf16(silu(g)) * u) with the hardware exp2 / reciprocal approximations for silu. Correct rounding
+        // of silu (the standalone kernel's silu_for_bf16) was measured here at 1.25-1.5x the time of the whole
+        // gate/up GEMM: this epilogue sits just under the mainloop's per-tile time, and with 2048 values per warp and
+        // tile most warp-tiles meet a value near a bf16 midpoint whose fp64 recomputation then stalls the warp.
+        // The fast form equals the correctly rounded silu except within a few fp32 ulp of a bf16 rounding midpoint:
+        // none of the 35.7 M values of configs[1] differs (tests/test_gemm_gpu.py counts them).
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const uint32_t gp = hp[i], up = upk[i];
@@ -1205,8 +1211,10 @@ tfb_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   // Persistent grid: as many groups as can be resident at once. A CTA pair must sit inside one GPC, so on parts
   // whose GPCs hold an odd number of usable SMs fewer than sm_count / 2 pairs fit; a larger grid would run its
   // extra pairs as a second wave after the first ones finished all their tiles.
-  static int resident[64];
-  if (!resident[di->device]) {
+  // (set-up calls from several host threads may race; they store the same value)
+  static std::atomic<int> resident[64];
+  int res = resident[di->device].load(std::memory_order_acquire);
+  if (!res) {
     TFB_CUDA(cudaFuncSetAttribute(gemm_kernel<MODE, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   Cfg<MODE, CG>::SMEM));
     int n = di->sm_count;
@@ -1215,9 +1223,10 @@ tfb_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
       TFB_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_kernel<MODE, CG>, &cfg));
       if (n <= 0) return fail(TFB_CUDA_ERR, "gemm: no CTA pair of this kernel fits on the device");
     }
-    resident[di->device] = min(n, di->sm_count / CG);
+    res = min(n, di->sm_count / CG);
+    resident[di->device].store(res, std::memory_order_release);
   }
-  const int groups = min(p.num_tiles, resident[di->device]);
+  const int groups = min(p.num_tiles, res);
   if (groups == 0) return TFB_OK;
   cfg.gridDim = dim3(groups * CG);
   TFB_CUDA(cudaLaunchKernelEx(&cfg, gemm_kernel<MODE, CG>, ta, tb, ty, p));
@@ -1235,11 +1244,10 @@ tfb_status check_common(int64_t M, int64_t N, int64_t K, const char* who) {
 
 // CTAs per MMA group: pairs (cta_group::2, 256-row tiles) unless M fits one 128-row tile or TFB_CTA_GROUP=1.
 int cta_group(int64_t M) {
-  static int forced = -1;
-  if (forced < 0) {
+  static const int forced = [] {   // read once (a function-local static is initialised thread-safely)
     const char* e = getenv("TFB_CTA_GROUP");
-    forced = e ? atoi(e) : 0;
-  }
+    return e ? atoi(e) : 0;
+  }();
   return (forced == 1 || M <= BM) ? 1 : 2;
 }
 
@@ -1563,10 +1571,17 @@ tfb_status gemm_nvfp4_swiglu(const uint8_t* a, const uint8_t* a_sf, const uint8_
   return dispatch<MODE_FP4_SWIGLU>(ta, tb, th, p, M, 128, F, s);
 }
 
+// FP8 takes the reference's FP8 envelope (tfimage/linear.py:159: K % 16 == 0, N % 16 == 0): the last K stage and
+// the last MMA k-block may be partly past K, and the last tile's B rows past N; TMA fills both with zeros, which add
+// nothing to the accumulator, and the output tensor map clips the stores at N.
 tfb_status gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, int64_t K, const float* a_scale,
                     const float* b_scale, int per_channel, void* y, int64_t ldy, cudaStream_t s) {
-  tfb_status st = check_common(M, N, K, "gemm_fp8");
-  if (st != TFB_OK) return st;
+  if (M < 0 || N <= 0 || K <= 0 || K % 16 || N % 16)
+    return fail(TFB_BAD_SHAPE, "gemm_fp8: need K %% 16 == 0 and N %% 16 == 0 (M=%lld N=%lld K=%lld)", (long long)M,
+                (long long)N, (long long)K);
+  if (M > (int64_t)1 << 30 || N > (int64_t)1 << 30 || K > (int64_t)1 << 30)
+    return fail(TFB_BAD_SHAPE, "gemm_fp8: dimension too large");
+  tfb_status st = TFB_OK;
   if (ldy < N || ldy % 8 || !aligned(y, 16) || !aligned(a_scale, 4) || !aligned(b_scale, 4))
     return fail(TFB_BAD_ALIGN, "gemm_fp8: y/ldy need 16-byte alignment");
   const DeviceInfo* di;
@@ -1580,8 +1595,8 @@ tfb_status gemm_fp8(const uint8_t* a, const uint8_t* b, int64_t M, int64_t N, in
   Params p{};
   p.M = (int)M;
   p.N = (int)N;
-  p.num_ks = (int)(K / 128);
-  p.kb_total = (int)(K / 32);
+  p.num_ks = (int)((K + 127) / 128);
+  p.kb_total = (int)((K + 31) / 32);
   p.b_rows = (int)N;
   p.y = y;
   p.ldy = ldy;

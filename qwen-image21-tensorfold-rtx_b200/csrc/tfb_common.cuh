@@ -144,6 +144,38 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// silu(g) = g / (1 + e^-g), rounded to bf16 (kernels.py:80 rounds silu to bf16 before the product) CORRECTLY: the
+// result is the round-to-nearest-even bf16 of the exact silu(g), so every implementation that rounds correctly --
+// the float64 oracle included -- agrees bit for bit (the standalone SwiGLU kernel). Two parts:
+//   * silu_fast_flag: branch-free fp32 with the hardware approximations, plus a flag. __expf(x) is within
+//     2 + floor(1.173 |x|) ulp of e^x (CUDA's documented bound), the add within 1/2 ulp, __fdividef within 2 ulp,
+//     so s is within 9 + 2.35 |g| ulp of the exact value: 19 ulp for |g| <= 4, 47 ulp for |g| <= 16. bf16
+//     rounding depends only on the low 16 bits of the fp32 pattern; when those lie more than 20 (|g| <= 4) or 60
+//     (|g| <= 16) ulp from the rounding midpoint 0x8000, the exact value rounds the same way. Otherwise, and for
+//     every |g| > 16, the flag is set (about one value in 1600 for typical gate values);
+//   * silu_f64_rto: the flagged values in fp64, rounded to fp32 by round-to-odd (truncate, set the last bit if
+//     inexact). fp32 keeps 16 more significand bits than bf16, so the later round-to-nearest-even to bf16 equals a
+//     single rounding of the fp64 value.
+__device__ __forceinline__ float silu_fast_flag(float g, bool& flag) {
+  const float s = __fdividef(g, 1.0f + __expf(-g));
+  const float a = fabsf(g);
+  const uint32_t w = a <= 4.0f ? 20u : 60u;
+  flag = ((__float_as_uint(s) & 0xFFFFu) - (0x8000u - w)) <= 2u * w || a > 16.0f;
+  return s;
+}
+static __device__ __noinline__ float silu_f64_rto(float g) {
+  const double d = (double)g / (1.0 + exp(-(double)g));
+  float f = __double2float_rz(d);
+  if ((double)f != d) f = __uint_as_float(__float_as_uint(f) | 1u);
+  return f;
+}
+// One value: an fp32 number whose bf16 rounding is the correctly rounded silu(g).
+__device__ __forceinline__ float silu_for_bf16(float g) {
+  bool flag;
+  const float s = silu_fast_flag(g, flag);
+  return flag ? silu_f64_rto(g) : s;
+}
+
 __device__ __forceinline__ void unpack_bf16x8(const uint4& u, float* f) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll

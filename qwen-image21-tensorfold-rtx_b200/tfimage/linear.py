@@ -10,8 +10,8 @@ Differences from the reference, all forced by the hardware or by the absent Tens
   * ``nvfp4_supported`` gates on compute capability 10.0 and on libtfb loading (the reference gates on 12.x);
   * the ``Fp4Linear`` container keeps the reference attribute names but its own layout: ``words`` are the NVFP4
     codes viewed as int32 [N, K/8], ``bs`` the scale bytes in the GEMM's tiled layout;
-  * NVFP4 needs ``k % 128 == 0 and n % 64 == 0`` (as in the reference); the FP8 GEMM needs ``k % 128 == 0 and
-    n % 32 == 0`` (the reference's cuBLASLt path took ``% 16``), other shapes go to bf16 as before;
+  * ``make`` dispatches exactly as the reference: NVFP4 needs ``k % 128 == 0 and n % 64 == 0``, FP8
+    ``k % 16 == 0 and n % 16 == 0``, other shapes go to bf16;
   * ``Fp8Linear`` optionally takes per-output-channel weight scales (``per_channel=True``).
 """
 
@@ -265,9 +265,11 @@ def swiglu_mlp(gate_up: Linear, down: Linear, x: torch.Tensor, residual=None):
     those codes. The hidden activations never exist in bf16 in HBM.
 
     Returns None (and the caller takes the unfused path, as with the reference) unless both layers are NVFP4 with
-    static input scales and ``down.k`` equals the hidden width F, a multiple of 64. ``residual=(res, gate)`` (this
-    build's addition): the down GEMM adds ``gate * y`` into ``res`` in place (``res.addcmul_(y, gate)``) and
-    ``res`` is returned."""
+    static input scales and ``down.k`` equals the hidden width F. The reference also asks F % 64 == 0; the GEMMs here
+    need F % 128 == 0, which every NVFP4 ``down`` from ``make`` satisfies (it has k % 128 == 0, and k = F), so the
+    fused path is taken for exactly the layer pairs the reference fuses. ``residual=(res, gate)`` (this build's
+    addition): the down GEMM adds ``gate * y`` into ``res`` in place (``res.addcmul_(y, gate)``) and ``res`` is
+    returned."""
 
     if not (isinstance(gate_up, Nvfp4Linear) and isinstance(down, Nvfp4Linear)) or gate_up.dynamic or down.dynamic:
         return None
@@ -354,6 +356,6 @@ def make(kind: str, w: torch.Tensor, act: float | None = None) -> Linear:
     n, k = w.shape
     if kind == "nvfp4" and nvfp4_supported() and k % 128 == 0 and n % 64 == 0:
         return Nvfp4Linear(w, act)
-    if kind in ("nvfp4", "fp8") and k % 128 == 0 and n % 32 == 0:
+    if kind in ("nvfp4", "fp8") and k % 16 == 0 and n % 16 == 0:
         return Fp8Linear(w, act)
     return Bf16Linear(w)

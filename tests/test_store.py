@@ -102,3 +102,10 @@ def test_reloaded_nvfp4_layer_is_identical(tmp_path, dev):
     x = bf16_cpu((200, 512), seed=10).to(dev)
     assert torch.equal(lin(x), back(x))
     assert np.array_equal(lin.lin.bs.cpu().numpy(), back.lin.bs.cpu().numpy())
+
+
+def test_model_level_functions_name_the_missing_reference_modules(tmp_path):
+    """store.load / load_or_convert build the reference's QwenImage21; without its modules in the package the
+    error says what to install."""
+    with pytest.raises(ImportError, match="qwen_image21.py"):
+        store.load(tmp_path / "missing.safetensors", device="cpu")

@@ -1,4 +1,4 @@
-"""Tensor-parallel MLP host logic on the CPU: world size 2 over gloo, each rank running the oracle on its shard
+"""Tensor-parallel MLP host logic on the CPU: world sizes 2 and 4 over gloo, each rank running the oracle on its shard
 (tfimage.tp's shards of the weight containers), the partial outputs all-reduced. Checks that a rank's NVFP4 SwiGLU
 codes / scales are exactly the corresponding columns of the unsharded ones and that the reduced output equals the
 unsharded oracle up to the bf16 rounding of the partials."""
@@ -75,8 +75,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_tp_mlp_shards_over_gloo(tmp_path):
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_mlp_shards_over_gloo(tmp_path, world):
     mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
     errs = [float((tmp_path / f"rank{r}.txt").read_text()) for r in range(world)]
     assert len(errs) == world and max(errs) <= 4e-3
@@ -96,9 +96,9 @@ def test_shards_reassemble_the_unsharded_containers():
         assert torch.equal(torch.cat([s.scales().view(torch.uint8) for s in ds_], 1), dn.scales().view(torch.uint8))
 
 
-def test_p2p_comm_refuses_unvalidated_group_sizes(tmp_path):
-    """The fused peer-memory path is validated for 2 ranks: a group of another size is refused before any buffer is
-    made (checked with a 1-rank gloo group, no GPU involved)."""
+def test_p2p_comm_refuses_a_one_rank_group(tmp_path):
+    """A peer-memory communicator needs 2 to 8 ranks (TFB_TP_MAX_WORLD): a 1-rank group is refused before any buffer
+    is made (no GPU involved)."""
     import socket
 
     import torch.distributed as dist
@@ -110,7 +110,7 @@ def test_p2p_comm_refuses_unvalidated_group_sizes(tmp_path):
         port = s.getsockname()[1]
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
     try:
-        with pytest.raises(ValueError, match="2 ranks"):
+        with pytest.raises(ValueError, match="2 to 8 ranks"):
             tp.P2PComm(4096, 3072)
     finally:
         dist.destroy_process_group()
