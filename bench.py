@@ -38,8 +38,8 @@ FLOP_STEP = FLOP_GU + FLOP_DOWN
 # fractions are against these nominal numbers).
 FP4_NOMINAL_TFLOPS, FP8_NOMINAL_TFLOPS = 9000.0, 4500.0
 # DRAM bytes per gate/up launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of this launch
-# (1.03 x its 35.8 MB of algorithmic operand bytes).
-TRAFFIC_GU = 36.87e6
+# (35.89 MB read + 1.70 MB written: 1.05 x its 35.8 MB of algorithmic operand bytes).
+TRAFFIC_GU = 37.59e6
 WORKLOAD = ("configs[1] fused NVFP4 MLP pair: X bf16 [4352,3072] N(0,1) -> gate/up W [16384,3072] N(0,0.02) with "
             "SwiGLU->NVFP4 epilogue -> down W [3072,8192] N(0,0.02) -> bf16 [4352,3072]")
 
