@@ -206,6 +206,54 @@ def cpu_baseline_fusions(budget_s: float = 4.0, rows: int = 256) -> dict:
             "sample": f"{rows} rows per call (numpy restatement of kernels.py:14-70 + the NVFP4 quantizer)"}
 
 
+def cpu_baseline_linears(budget_s: float = 4.0, rows: int = 128) -> dict:
+    """configs[0] and configs[3] on the host cores: the reference's CPU linear paths as restated in oracle/ -- NVFP4
+    (quantize + dequantize the X rows under the dynamic global, fp32 matmul against the dequantized weight, bf16;
+    tools/gemm_tf.py:21-24) and FP8 W8A8 (per-tensor e4m3 activation, per-channel weight scales, fp32 matmul, bf16;
+    tfimage/linear.py:86-100) -- on ``rows`` rows per call, weights quantized and dequantized once outside the timing,
+    reported as TFLOP/s of those rows."""
+    import numpy as np
+    import torch
+
+    from oracle import fp8 as ofp8
+    from oracle import nvfp4 as onv
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(29)
+    K = N = 3072
+    x = rng.standard_normal((rows, K)).astype(np.float32)
+    x[:, rng.permutation(K)[:8]] *= 20
+    x = onv.bf16_round(x)
+    w = onv.bf16_round((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+    gw = onv.weight_global(float(np.abs(w).max()))
+    wd = torch.from_numpy(onv.dequantize(*onv.quantize(w, gw), gw))
+    w8, ws = ofp8.weight(w, per_channel=True)
+    w8d = torch.from_numpy(onv.e4m3_decode(w8).astype(np.float32))
+
+    def run(fn):
+        fn()
+        n, t0 = 0, time.perf_counter()
+        while n == 0 or time.perf_counter() - t0 < budget_s / 2:
+            fn()
+            n += 1
+        return (time.perf_counter() - t0) / n
+
+    def nvfp4():
+        ga = onv.dynamic_act_global(float(np.abs(x).max()))
+        xd = torch.from_numpy(onv.dequantize(*onv.quantize(x, ga), ga))
+        return onv.bf16_round((xd @ wd.T).numpy())
+
+    def fp8():
+        a = ofp8.act_scale(x)
+        xq = torch.from_numpy(onv.e4m3_decode(ofp8.quantize(x, a)).astype(np.float32))
+        return onv.bf16_round(((xq @ w8d.T) * (float(a) * torch.from_numpy(np.asarray(ws, np.float32)))).numpy())
+
+    flop = 2 * rows * K * N
+    return {"c0_nvfp4_tflops": flop / run(nvfp4) / 1e12, "c3_fp8_tflops": flop / run(fp8) / 1e12,
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{rows} of the 4096 (configs[0]) / 4968 (configs[3]) rows per call, [3072, 3072] weight"}
+
+
 def _sdpa_cpu(q, k, v, causal=False):
     """The reference's attention op (torch SDPA) on the host cores in fp32, for the CPU block timing."""
     import numpy as np
@@ -339,14 +387,25 @@ def config_legs(dev, fp4_peak: float, fp8_peak: float, hbm_gbs: float) -> dict:
     lin.set_act(float(_lib.absmax(x0)) / (6 * 448))
     q0 = lin.quantize(x0)
     t_gemm, t_quant = timed(lambda: lin(q0)), timed(lambda: lin.quantize(x0))
+    # end to end from pinned host rows: X in, quantize + GEMM, Y out, one after the other on the stream
+    x0_host = x0.cpu().pin_memory()
+    y0_host = torch.empty((M0, K0), dtype=torch.bfloat16).pin_memory()
+    x0_dev = torch.empty_like(x0)
+
+    def e2e0():
+        x0_dev.copy_(x0_host, non_blocking=True)
+        y0_host.copy_(lin(x0_dev), non_blocking=True)
+    t_e2e0 = timed(e2e0)
     flop0 = 2 * M0 * K0 * K0
     qbytes = M0 * K0 * 2 + M0 * K0 // 2 + M0 * K0 // 16
     out["configs[0]"] = {
         "workload": "NVFP4 W4A4 linear: X bf16 [4096, 3072] N(0,1), 8 channels x20; W [3072, 3072] N(0, 0.02)",
         "gemm_us": t_gemm, "gemm_tflops": flop0 / t_gemm / 1e6, "gemm_frac_fp4_peak": flop0 / t_gemm / 1e6 / fp4_peak,
         "quant_us": t_quant, "quant_gbs": qbytes / t_quant / 1e3, "quant_frac_hbm": qbytes / t_quant / 1e3 / hbm_gbs,
-        "linear_tflops": flop0 / (t_gemm + t_quant) / 1e6}
-    del x0, lin, q0
+        "linear_tflops": flop0 / (t_gemm + t_quant) / 1e6,
+        "e2e": {"us": t_e2e0, "tflops": flop0 / t_e2e0 / 1e6, "h2d_bytes": M0 * K0 * 2, "d2h_bytes": M0 * K0 * 2,
+                "path": "pinned X -> device copy, Nvfp4Linear (quantize + GEMM), bf16 Y -> pinned host copy, in order"}}
+    del x0, lin, q0, x0_host, y0_host, x0_dev
 
     # AdaLN(+shift) + NVFP4 quantize on x [4352, 3072]; RMSNorm + RoPE of q, k (+ v) from qkv
     M2, D = 4352, 3072
@@ -538,7 +597,7 @@ def summary(line: dict) -> dict:
         c0, c2, c3 = cf["configs[0]"], cf["configs[2]"], cf["configs[3]"]
         out.update(c0_gemm_us=r(c0["gemm_us"], 2), c0_gemm_tflops=r(c0["gemm_tflops"], 1),
                    c0_frac_fp4=r(c0["gemm_frac_fp4_peak"]), c0_quant_us=r(c0["quant_us"], 2),
-                   c0_linear_tflops=r(c0["linear_tflops"], 1),
+                   c0_linear_tflops=r(c0["linear_tflops"], 1), c0_e2e_tflops=r(c0["e2e"]["tflops"], 1),
                    c2_adaln_quant_gbs=r(c2["adaln_quant_gbs"], 0), c2_adaln_quant_frac=r(c2["adaln_quant_frac_hbm"]),
                    c2_rope_qkv_gbs=r(c2["rms_rope_qkv_gbs"], 0), c2_rope_qkv_frac=r(c2["rms_rope_qkv_frac_hbm"]),
                    c3_fp8_tflops=[r(c3[k]["tflops"], 0) for k in ("linear_3072", "gate_up_16384", "down_3072_k8192")],
@@ -556,6 +615,9 @@ def summary(line: dict) -> dict:
         out["cpu_c1_tflops"] = r(cb["value"], 4)
     if line.get("cpu_baseline_configs2"):
         out["cpu_c2_adaln_quant_gbs"] = r(line["cpu_baseline_configs2"]["adaln_quant_gbs"])
+    if line.get("cpu_baseline_configs0_3"):
+        out["cpu_c0_tflops"] = r(line["cpu_baseline_configs0_3"]["c0_nvfp4_tflops"], 4)
+        out["cpu_c3_fp8_tflops"] = r(line["cpu_baseline_configs0_3"]["c3_fp8_tflops"], 4)
     if line.get("cpu_baseline_configs4"):
         out["cpu_c4_step_s"] = r(line["cpu_baseline_configs4"]["step_s_estimate"], 1)
     hl = line["e2e"].get("host_link", {})
@@ -788,6 +850,7 @@ def run_ours(args):
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
             line["cpu_baseline_configs2"] = cpu_baseline_fusions()
+            line["cpu_baseline_configs0_3"] = cpu_baseline_linears()
             if dit_model is not None:
                 line["cpu_baseline_configs4"] = cpu_baseline_dit(*dit_model)
         line["summary"] = summary(line)

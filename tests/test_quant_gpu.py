@@ -24,7 +24,7 @@ def tie_rows():
     return np.tile(row, (4, 4)), 1.0 / 8
 
 
-@pytest.mark.parametrize("M,K", [(1, 64), (300, 192), (4096, 3072)])
+@pytest.mark.parametrize("M,K", [(1, 64), (300, 192), (77, 448), (4096, 3072), (20000, 1344)])
 @pytest.mark.parametrize("layout", [_lib.SF_ROWS, _lib.SF_TILED])
 def test_quant_nvfp4_bit_exact(dev, M, K, layout):
     x = bf16_cpu((M, K), seed=M + K, outliers=8)
@@ -36,6 +36,17 @@ def test_quant_nvfp4_bit_exact(dev, M, K, layout):
         np.testing.assert_array_equal(u8(sf), rs)
     else:
         np.testing.assert_array_equal(u8(sf), onv.sf_tile(rs))       # padded rows included (zero)
+
+
+@pytest.mark.parametrize("M,K", [(130, 80), (33, 336), (5, 16)])
+def test_quant_nvfp4_rows_layout_ragged_segments(dev, M, K):
+    """Row-major scales for K a multiple of 16 only: the last 256-element segment of each row is partial."""
+    x = bf16_cpu((M, K), seed=3 * M + K, outliers=2)
+    g = onv.dynamic_act_global(float(x.float().abs().max()))
+    codes, sf = _lib.quant_nvfp4(x.to(dev), g, _lib.SF_ROWS)
+    rc, rs = onv.quantize(x.float().numpy(), g)
+    np.testing.assert_array_equal(u8(codes), rc)
+    np.testing.assert_array_equal(u8(sf), rs)
 
 
 def test_quant_nvfp4_rounding_midpoints(dev):
