@@ -491,6 +491,9 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
   if (CG == 2) asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
   const int grp = blockIdx.x / CG, ngrp = gridDim.x / CG;
   if (threadIdx.x == 0) {
+    // the operand maps are kernel parameters, not outputs of the previous kernel: fetch them before pdl_wait
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
     for (int s = 0; s < STAGES; ++s) {
       // leader: its producer's arrive (with the tile bytes of the group) + every scale warp of the group
       mbar_init(full + s, 1 + (FP4 ? 4 * CG : 0));
@@ -542,8 +545,6 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ----------------------------------------------------------------------------------------- producer
-      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
       int stage = 0;
       uint32_t ph = 0;
       uint32_t issued = 0;     // bit s: stage s was armed at least once
