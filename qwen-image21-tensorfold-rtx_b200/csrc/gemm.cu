@@ -454,8 +454,10 @@ struct Cfg {
   static constexpr int B_BYTES_CTA = CG == 2 ? 128 * BKB : BN * BKB;
   static constexpr int SF_BYTES = MODE == 1 ? 0 : SFA_BYTES + SFB_BYTES;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES_CTA + SF_BYTES;
-  static constexpr int STAGES = CG == 2 ? (MODE == 1 ? 6 : 5) : (MODE == 1 ? 4 : 3);
-  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + OUT_BYTES + 512;
+  static constexpr int STAGES = CG == 2 ? 5 : 3;
+  // FP8: each epilogue warp stages its 128 per-channel weight scales (512 B) before the accumulator is ready
+  static constexpr int SC_BYTES = MODE == 1 ? 8 * 128 * 4 : 0;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + OUT_BYTES + SC_BYTES + 512;
 };
 
 template <int MODE, int CG>
@@ -475,7 +477,8 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
   uint8_t* sOut = sSFB + (FP4 ? STAGES * SFB_BYTES : 0);
   // full: the stage's loads landed -- one CTA: all of them; a pair: the leader's copy counts both CTAs' operand
   // tiles (each CTA's tensor loads complete on it), the follower's is unused
-  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + OUT_BYTES);
+  float* sSC = reinterpret_cast<float*>(sOut + OUT_BYTES);   // FP8 per-channel scales, 128 per epilogue warp
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + OUT_BYTES + C::SC_BYTES);
   uint64_t* empty = full + STAGES;          // the stage's MMAs completed (commit from the group's MMA thread)
   uint64_t* sff = empty + STAGES;           // NVFP4: this CTA's scale bytes landed (its scale warps wait here)
   uint64_t* acc_full = sff + STAGES;
@@ -791,6 +794,9 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
                                    ? (uint32_t)CG * *reinterpret_cast<const volatile uint32_t*>(p.tp_epoch_dev)
                                    : p.tp_target;
     int sig_seq = 0;                              // TP: tiles handed to the signal warp so far
+    // FP8: the activation scale (and a per-tensor weight scale) for the whole launch, written by earlier kernels
+    const float fp8_scale =
+        MODE == MODE_FP8 ? __ldg(p.a_scale) * (p.b_per_channel ? 1.0f : __ldg(p.b_scale)) : 0.0f;
     auto sig_hand_off = [&]() {
       // slot reuse: the signal warp has finished the tile kSigSlots back
       if (sig_seq >= kSigSlots && lane == 0)
@@ -816,6 +822,15 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
         mbar_expect_tx(xb, OUT_WARP_BYTES);
         tma_load_2d(stg, &tmY, xb, nb * BN + half * 128, row0 + q * 32);
         x_pending = 1;
+      }
+      float* wsc = sSC + (warp - EPI_WARP0) * 128;
+      if (MODE == MODE_FP8 && p.b_per_channel) {
+        // this tile's 128 column scales of this warp, read while the MMAs run (zero past N); a per-element global
+        // load inside the drain below held the accumulator ~6 us per tile
+        const int nc = nb * BN + half * 128 + lane * 4;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) wsc[lane * 4 + k] = nc + k < p.N ? __ldg(p.b_scale + nc + k) : 0.0f;
+        __syncwarp();
       }
       if (!mbar_wait<false>(acc_full, acc_ph, p.err, 0x301)) break;
       tc_fence_after();
@@ -905,30 +920,60 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0 && row0 + q * 32 < p.M) tma_store_2d(&tmY, stg, (int)(col0 / 2), row0 + q * 32);
+      } else if constexpr (MODE == MODE_FP8) {
+        // this warp: output columns [half*128, half*128 + 128) of the tile as two 64-column boxes, each drained,
+        // scaled (per-tensor, or per-channel from the scales staged above), rounded and stored in turn, so one box
+        // of registers suffices; the accumulator is released after the second box's TMEM reads
+        const int n_base = nb * BN + half * 128;
+#pragma unroll 1
+        for (int bx = 0; bx < 2; ++bx) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t raw[32];
+            const uint32_t t0 = trow + ACC_COL + half * 128 + bx * 64 + c * 32;
+            tmem_ld16x2(t0, t0 + 16, raw);
+            const float* w = wsc + bx * 64 + c * 32;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float v0 = __uint_as_float(raw[2 * j]) * fp8_scale, v1 = __uint_as_float(raw[2 * j + 1]) * fp8_scale;
+              if (p.b_per_channel) {
+                v0 *= w[2 * j];
+                v1 *= w[2 * j + 1];
+              }
+              pk[c * 16 + j] = pack_bf16x2(v0, v1);
+            }
+          }
+          if (bx == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {                       // drained: the next tile's MMAs may start
+              if (CG == 2 && rank != 0) mbar_arrive_cluster(acc_empty_l);
+              else mbar_arrive(acc_empty);
+            }
+          }
+          if (lane == 0) tma_store_wait_read();    // the staging box is free once the previous store read it
+          __syncwarp();
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch)
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
+                make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0 && rows_live && n_base + bx * 64 < p.N) tma_store_2d(&tmY, stg, n_base + bx * 64, row0 + q * 32);
+        }
       } else {
         // this warp: output columns [half*128, half*128 + 128) of the tile, drained 32 at a time
-        float scale = p.alpha;
-        if (MODE == MODE_FP8) scale = __ldg(p.a_scale) * (p.b_per_channel ? 1.0f : __ldg(p.b_scale));
+        const float scale = p.alpha;
         const int n_base = nb * BN + half * 128;
         uint32_t pk[64];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t raw[32];
           tmem_ld16x2(trow + ACC_COL + half * 128 + c * 32, trow + ACC_COL + half * 128 + c * 32 + 16, raw);
-          const int n0 = n_base + c * 32;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float v0 = __uint_as_float(raw[2 * j]), v1 = __uint_as_float(raw[2 * j + 1]);
-            if (MODE == MODE_FP8 && p.b_per_channel) {
-              const bool inb = n0 + 2 * j < p.N;
-              v0 *= scale * (inb ? __ldg(p.b_scale + n0 + 2 * j) : 0.0f);
-              v1 *= scale * (inb ? __ldg(p.b_scale + n0 + 2 * j + 1) : 0.0f);
-            } else {
-              v0 *= scale;
-              v1 *= scale;
-            }
-            pk[c * 16 + j] = pack_bf16x2(v0, v1);
-          }
+          for (int j = 0; j < 16; ++j)
+            pk[c * 16 + j] = pack_bf16x2(__uint_as_float(raw[2 * j]) * scale, __uint_as_float(raw[2 * j + 1]) * scale);
         }
         tc_fence_before();
         __syncwarp();
