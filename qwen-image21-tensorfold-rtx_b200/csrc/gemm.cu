@@ -797,6 +797,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
     // FP8: the activation scale (and a per-tensor weight scale) for the whole launch, written by earlier kernels
     const float fp8_scale =
         MODE == MODE_FP8 ? __ldg(p.a_scale) * (p.b_per_channel ? 1.0f : __ldg(p.b_scale)) : 0.0f;
+    (void)fp8_scale;
     auto sig_hand_off = [&]() {
       // slot reuse: the signal warp has finished the tile kSigSlots back
       if (sig_seq >= kSigSlots && lane == 0)
@@ -824,12 +825,14 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
         x_pending = 1;
       }
       float* wsc = sSC + (warp - EPI_WARP0) * 128;
-      if (MODE == MODE_FP8 && p.b_per_channel) {
-        // this tile's 128 column scales of this warp, read while the MMAs run (zero past N); a per-element global
-        // load inside the drain below held the accumulator ~6 us per tile
+      if constexpr (MODE == MODE_FP8) {
+        // this tile's output scale of each of this warp's 128 columns, a * ws[n] (per-channel weight scales) or a * ws,
+        // written while the MMAs run (zero past N); a per-element global load inside the drain held the accumulator
+        // ~6 us per tile
         const int nc = nb * BN + half * 128 + lane * 4;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) wsc[lane * 4 + k] = nc + k < p.N ? __ldg(p.b_scale + nc + k) : 0.0f;
+        for (int k = 0; k < 4; ++k)
+          wsc[lane * 4 + k] = nc + k < p.N ? (p.b_per_channel ? fp8_scale * __ldg(p.b_scale + nc + k) : fp8_scale) : 0.0f;
         __syncwarp();
       }
       if (!mbar_wait<false>(acc_full, acc_ph, p.err, 0x301)) break;
@@ -921,43 +924,38 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
         __syncwarp();
         if (lane == 0 && row0 + q * 32 < p.M) tma_store_2d(&tmY, stg, (int)(col0 / 2), row0 + q * 32);
       } else if constexpr (MODE == MODE_FP8) {
-        // this warp: output columns [half*128, half*128 + 128) of the tile as two 64-column boxes, each drained,
-        // scaled (per-tensor, or per-channel from the scales staged above), rounded and stored in turn, so one box
-        // of registers suffices; the accumulator is released after the second box's TMEM reads
+        // this warp: output columns [half*128, half*128 + 128) of the tile: all 128 drained to bf16 pairs (scaled
+        // per tensor, or per channel from the scales staged above) and the accumulator released before the two
+        // 64-column boxes go through the staging box to TMA stores
         const int n_base = nb * BN + half * 128;
-#pragma unroll 1
+        uint32_t pk[64];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t raw[32];
+          const uint32_t t0 = trow + ACC_COL + half * 128 + c * 32;
+          tmem_ld16x2(t0, t0 + 16, raw);
+          const float2* w = reinterpret_cast<const float2*>(wsc) + c * 16;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float2 w2 = w[j];
+            pk[c * 16 + j] = pack_bf16x2(__uint_as_float(raw[2 * j]) * w2.x, __uint_as_float(raw[2 * j + 1]) * w2.y);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {                           // drained: the next tile's MMAs may start
+          if (CG == 2 && rank != 0) mbar_arrive_cluster(acc_empty_l);
+          else mbar_arrive(acc_empty);
+        }
+#pragma unroll
         for (int bx = 0; bx < 2; ++bx) {
-          uint32_t pk[32];
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t raw[32];
-            const uint32_t t0 = trow + ACC_COL + half * 128 + bx * 64 + c * 32;
-            tmem_ld16x2(t0, t0 + 16, raw);
-            const float* w = wsc + bx * 64 + c * 32;
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              float v0 = __uint_as_float(raw[2 * j]) * fp8_scale, v1 = __uint_as_float(raw[2 * j + 1]) * fp8_scale;
-              if (p.b_per_channel) {
-                v0 *= w[2 * j];
-                v1 *= w[2 * j + 1];
-              }
-              pk[c * 16 + j] = pack_bf16x2(v0, v1);
-            }
-          }
-          if (bx == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {                       // drained: the next tile's MMAs may start
-              if (CG == 2 && rank != 0) mbar_arrive_cluster(acc_empty_l);
-              else mbar_arrive(acc_empty);
-            }
-          }
           if (lane == 0) tma_store_wait_read();    // the staging box is free once the previous store read it
           __syncwarp();
 #pragma unroll
           for (int ch = 0; ch < 8; ++ch)
             *reinterpret_cast<uint4*>(stg + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
-                make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+                make_uint4(pk[bx * 32 + 4 * ch], pk[bx * 32 + 4 * ch + 1], pk[bx * 32 + 4 * ch + 2],
+                           pk[bx * 32 + 4 * ch + 3]);
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
           if (lane == 0 && rows_live && n_base + bx * 64 < p.N) tma_store_2d(&tmY, stg, n_base + bx * 64, row0 + q * 32);
