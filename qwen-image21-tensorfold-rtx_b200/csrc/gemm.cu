@@ -456,7 +456,8 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES_CTA + SF_BYTES;
   static constexpr int STAGES = CG == 2 ? 5 : 3;
   // FP8: each epilogue warp stages its 128 per-channel weight scales (512 B) before the accumulator is ready
-  static constexpr int SC_BYTES = MODE == 1 ? 8 * 128 * 4 : 0;
+  // QKV: the q and k RMSNorm weights (2 x 128 floats), staged once per launch
+  static constexpr int SC_BYTES = MODE == 1 ? 8 * 128 * 4 : MODE == 5 ? 2 * 128 * 4 : 0;
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + OUT_BYTES + SC_BYTES + 512;
 };
 
@@ -477,7 +478,8 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
   uint8_t* sOut = sSFB + (FP4 ? STAGES * SFB_BYTES : 0);
   // full: the stage's loads landed -- one CTA: all of them; a pair: the leader's copy counts both CTAs' operand
   // tiles (each CTA's tensor loads complete on it), the follower's is unused
-  float* sSC = reinterpret_cast<float*>(sOut + OUT_BYTES);   // FP8 per-channel scales, 128 per epilogue warp
+  float* sSC = reinterpret_cast<float*>(sOut + OUT_BYTES);   // FP8: output scales, 128 per epilogue warp;
+                                                             // QKV: the q and k norm weights
   uint64_t* full = reinterpret_cast<uint64_t*>(sOut + OUT_BYTES + C::SC_BYTES);
   uint64_t* empty = full + STAGES;          // the stage's MMAs completed (commit from the group's MMA thread)
   uint64_t* sff = empty + STAGES;           // NVFP4: this CTA's scale bytes landed (its scale warps wait here)
@@ -798,6 +800,12 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
     const float fp8_scale =
         MODE == MODE_FP8 ? __ldg(p.a_scale) * (p.b_per_channel ? 1.0f : __ldg(p.b_scale)) : 0.0f;
     (void)fp8_scale;
+    if constexpr (MODE == MODE_FP4_QKV) {
+      // the q and k norm weights for every tile of the launch (the 8 epilogue warps fill them; named barrier 1)
+      const int et = threadIdx.x - EPI_WARP0 * 32;
+      sSC[et] = __ldg(p.qk_w[et >> 7] + (et & 127));
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+    }
     auto sig_hand_off = [&]() {
       // slot reuse: the signal warp has finished the tile kSigSlots back
       if (sig_seq >= kSigSlots && lane == 0)
@@ -1005,9 +1013,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
             rr = rms_rr(__fadd_rn(a8[0], a8[1]), p.qk_eps);
           }
           __nv_bfloat16* dst = p.qk_dst[part] + (int64_t)bb * p.qk_sb[part] + (int64_t)head * 128;
-          const float* w = p.qk_w[part < 2 ? part : 0];
-          const float* cs = p.qk_cos + (int64_t)(n0 + lane) * 64;
-          const float* sn = p.qk_sin + (int64_t)(n0 + lane) * 64;
+          const float* w = sSC + (part == 1 ? 128 : 0);
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             __syncwarp();
@@ -1016,31 +1022,30 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
               *reinterpret_cast<uint4*>(stg + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
                   make_uint4(pk[c * 32 + 4 * ch], pk[c * 32 + 4 * ch + 1], pk[c * 32 + 4 * ch + 2],
                              pk[c * 32 + 4 * ch + 3]);
-            if (norm) {
-              // weight and RoPE on this thread's row of the box, 8 values at a time, in place in shared memory
-#pragma unroll 1
-              for (int j = 0; j < 8; ++j) {
-                uint4* px = reinterpret_cast<uint4*>(stg + lane * 128 + ((j ^ (lane & 7)) << 4));
+            __syncwarp();
+            // 4 rows x 128 B per pass: lane (r % 4) * 8 + ck takes chunk ck (8 values) of row r, so the row's cos /
+            // sin (fp32, 64 per token) and the stores into the part's destination rows are both contiguous per 8
+            // lanes; the row's RMS factor comes from the lane that summed it
+#pragma unroll 2
+            for (int i = 0; i < 8; ++i) {
+              const int r = i * 4 + (lane >> 3), ck = lane & 7;
+              const float rr_r = __shfl_sync(0xffffffffu, rr, r);
+              const bool row_live = grow0 + r < p.M;
+              uint4 o = *reinterpret_cast<const uint4*>(stg + r * 128 + ((ck ^ (r & 7)) << 4));
+              if (part < 2 && row_live) {
                 float x[8];
-                unpack_bf16x8(*px, x);
-                const int jj = c * 8 + j;
-                const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + jj * 8));
-                const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + jj * 8 + 4));
-                const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + jj * 4));
-                const float4 s4 = __ldg(reinterpret_cast<const float4*>(sn + jj * 4));
+                unpack_bf16x8(o, x);
+                const int jj = c * 8 + ck;
+                const float4 w0 = *reinterpret_cast<const float4*>(w + jj * 8);
+                const float4 w1 = *reinterpret_cast<const float4*>(w + jj * 8 + 4);
+                const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.qk_cos + (int64_t)(n0 + r) * 64 + jj * 4));
+                const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.qk_sin + (int64_t)(n0 + r) * 64 + jj * 4));
                 const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
                 const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
-                *px = norm_rope8(x, rr, wv, cv, sv);
+                o = norm_rope8(x, rr_r, wv, cv, sv);
               }
-            }
-            __syncwarp();
-            // coalesced 16-byte stores, 4 rows x 128 B per pass, into the part's destination rows
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int rr2 = i * 4 + (lane >> 3), ck = lane & 7;
-              if (grow0 + rr2 < p.M && n_base + c * 64 < p.N)
-                *reinterpret_cast<uint4*>(dst + (int64_t)(n0 + rr2) * p.qk_sn[part] + c * 64 + ck * 8) =
-                    *reinterpret_cast<const uint4*>(stg + rr2 * 128 + ((ck ^ (rr2 & 7)) << 4));
+              if (row_live && n_base + c * 64 < p.N)
+                *reinterpret_cast<uint4*>(dst + (int64_t)(n0 + r) * p.qk_sn[part] + c * 64 + ck * 8) = o;
             }
           }
           __syncwarp();
