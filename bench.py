@@ -627,7 +627,7 @@ def summary(line: dict) -> dict:
 
 
 # --------------------------------------------------------------------------------------------- profile legs
-PROFILE_LEGS = ("gemm0", "fp8_3072", "adaln_quant", "swiglu")
+PROFILE_LEGS = ("gemm0", "fp8_3072", "adaln_quant", "swiglu", "qkv")
 
 
 def run_profile_leg(name: str, reps: int = 4) -> None:
@@ -637,6 +637,8 @@ def run_profile_leg(name: str, reps: int = 4) -> None:
       fp8_3072     configs[3] FP8 GEMM     X e4m3 [4968, 3072] x W [3072, 3072], per-channel W scales
       adaln_quant  configs[2] AdaLN + shift + NVFP4 quantize on x [4352, 3072]
       swiglu       configs[1] gate/up NVFP4 GEMM with the SwiGLU -> NVFP4 epilogue (M 4352, F 8192, K 3072)
+      qkv          configs[4] qkv NVFP4 GEMM with q / k RMSNorm + RoPE and the v copy in its epilogue (4096 tokens,
+                   24 heads of 128, K 3072)
     Prints one line per launch with its CUDA-event time (for orientation only; never a bench value)."""
     import torch
 
@@ -671,6 +673,19 @@ def run_profile_leg(name: str, reps: int = 4) -> None:
         q = gu.quantize(x)
         fn = lambda: _lib.gemm_nvfp4_swiglu(q.codes, q.sf, gu.lin.codes, gu.lin.bs, 4352, 8192, 3072,  # noqa: E731
                                              q.act * gu.lin.scale, 0.004)
+    elif name == "qkv":
+        x = torch.randn(4096, 3072, generator=g).to(torch.bfloat16).to(dev)
+        w = L.Nvfp4Linear((torch.randn(9216, 3072, generator=g) * 0.02).to(torch.bfloat16).to(dev))
+        w.set_act(float(_lib.absmax(x)) / (6 * 448))
+        q = w.quantize(x)
+        qo = torch.empty(1, 4096, 24, 128, dtype=torch.bfloat16, device=dev)
+        ko, vo = torch.empty_like(qo), torch.empty_like(qo)
+        wq = (torch.randn(128, generator=g) * 0.05 + 1).to(dev)
+        wk = (torch.randn(128, generator=g) * 0.05 + 1).to(dev)
+        ang = torch.rand(4096, 64, generator=g).to(dev) * 6.28
+        cos, sin = torch.cos(ang), torch.sin(ang)
+        fn = lambda: _lib.gemm_nvfp4_qkv(q.codes, q.sf, w.lin.codes, w.lin.bs, 1, 4096, 24, 3072,  # noqa: E731
+                                         q.act * w.lin.scale, wq, wk, cos, sin, 1e-6, qo, ko, vo)
     else:
         raise SystemExit(f"unknown profile leg {name!r}; one of {PROFILE_LEGS}")
     stream = torch.cuda.current_stream(dev)
