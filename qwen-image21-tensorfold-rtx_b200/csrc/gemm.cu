@@ -483,9 +483,12 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(sOut + OUT_BYTES + C::SC_BYTES);
   uint64_t* empty = full + STAGES;          // the stage's MMAs completed (commit from the group's MMA thread)
   uint64_t* sff = empty + STAGES;           // NVFP4: this CTA's scale bytes landed (its scale warps wait here)
-  uint64_t* acc_full = sff + STAGES;
-  uint64_t* acc_empty = acc_full + 1;       // leader: every epilogue warp of the group drained the accumulator
-  uint64_t* drain = acc_empty + 1;
+  // FP8 has no scales in TMEM, so its accumulator is double-buffered (columns [0, 256) and [256, 512), tile t in
+  // buffer t % 2): the next tile's MMAs run while the epilogue drains the previous tile
+  constexpr int NACC = MODE == MODE_FP8 ? 2 : 1;
+  uint64_t* acc_full = sff + STAGES;        // per accumulator buffer
+  uint64_t* acc_empty = acc_full + 2;       // leader: every epilogue warp of the group drained the buffer
+  uint64_t* drain = acc_empty + 2;
   uint64_t* xbar = drain + 1;               // resid: per epilogue warp, its residual box landed in its staging
   uint64_t* sigbar = xbar + 8;              // TP: every epilogue warp finished the tile's stores (ring of slots)
   uint64_t* ackbar = sigbar + kSigSlots;    // TP: the signal warp has signalled that slot's tile
@@ -505,8 +508,10 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
       mbar_init(empty + s, 1);
       mbar_init(sff + s, 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 8 * CG);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, 8 * CG);
+    }
     mbar_init(drain, 1);
     for (int w = 0; w < 8; ++w) mbar_init(xbar + w, 1);
     for (int k = 0; k < kSigSlots; ++k) {
@@ -642,12 +647,14 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
       // spends between stages is at risk of idling it. Descriptors advance arithmetically (start address >> 4).
       const uint64_t dA0 = desc_sw128(sA), dB0 = desc_sw128(sB);
       const uint32_t full0 = smem_u32(full), empty0 = smem_u32(empty);
-      const uint32_t dacc = tmem + ACC_COL;
-      int stage = 0;
-      uint32_t ph = 0, acc_ph = 0;
+      int stage = 0, acc_t = 0;                    // acc_t: this CTA's tiles so far
+      uint32_t ph = 0;
       bool ok = true;
-      for (int tile = grp; ok && tile < p.num_tiles; tile += ngrp) {
-        if (!mbar_wait<true>(acc_empty, acc_ph ^ 1, p.err, 0x201)) {
+      for (int tile = grp; ok && tile < p.num_tiles; tile += ngrp, ++acc_t) {
+        const int ab = acc_t % NACC;
+        const uint32_t acc_ph = (uint32_t)(acc_t / NACC) & 1;
+        const uint32_t dacc = tmem + ACC_COL + ab * 256;
+        if (!mbar_wait<true>(acc_empty + ab, acc_ph ^ 1, p.err, 0x201)) {
           ok = false;
           break;
         }
@@ -685,8 +692,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
           }
         }
         if (!ok) break;
-        tc_commit<CG>(smem_u32(acc_full));
-        acc_ph ^= 1;
+        tc_commit<CG>(smem_u32(acc_full + ab));
       }
       // drain: the commit arrives once every tcgen05 op this thread issued has completed
       tc_commit_local<CG>(smem_u32(drain));
@@ -786,7 +792,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
     const int r = q * 32 + lane;                   // row inside this CTA's 128 rows == TMEM lane
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
     uint8_t* stg = sOut + (warp - EPI_WARP0) * OUT_WARP_BYTES;   // this warp's 32 x 128-byte staging box
-    uint32_t acc_ph = 0;
+    int acc_t = 0;                                // this CTA's tiles so far (accumulator buffer and phase)
     uint64_t* xb = xbar + (warp - EPI_WARP0);
     uint32_t x_ph = 0, x_pending = 0;             // resid: parity of the next load; a load not yet waited for
     constexpr bool kResidMode = MODE == MODE_FP4_RESID || MODE == MODE_FP4_TP;
@@ -843,7 +849,8 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
           wsc[lane * 4 + k] = nc + k < p.N ? (p.b_per_channel ? fp8_scale * __ldg(p.b_scale + nc + k) : fp8_scale) : 0.0f;
         __syncwarp();
       }
-      if (!mbar_wait<false>(acc_full, acc_ph, p.err, 0x301)) break;
+      const int ab = acc_t % NACC;                 // this tile's accumulator buffer
+      if (!mbar_wait<false>(acc_full + ab, (uint32_t)(acc_t / NACC) & 1, p.err, 0x301)) break;
       tc_fence_after();
       if (MODE == MODE_FP4_SWIGLU) {
         // this warp: hidden columns [half*64, half*64 + 64) of the tile = gate and up accumulator columns
@@ -869,8 +876,8 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {                           // drained: the next tile's MMAs may start
-          if (CG == 2 && rank != 0) mbar_arrive_cluster(acc_empty_l);
-          else mbar_arrive(acc_empty);
+          if (CG == 2 && rank != 0) mbar_arrive_cluster(acc_empty_l + ab * 8);
+          else mbar_arrive(acc_empty + ab);
         }
         if (p.gu_out && m < p.M) {                 // test-only output: the bf16 gate/up values the math used
 #pragma unroll
@@ -940,7 +947,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t raw[32];
-          const uint32_t t0 = trow + ACC_COL + half * 128 + c * 32;
+          const uint32_t t0 = trow + ACC_COL + ab * 256 + half * 128 + c * 32;
           tmem_ld16x2(t0, t0 + 16, raw);
           const float2* w = reinterpret_cast<const float2*>(wsc) + c * 16;
 #pragma unroll
@@ -952,8 +959,8 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {                           // drained: the next tile's MMAs may start
-          if (CG == 2 && rank != 0) mbar_arrive_cluster(acc_empty_l);
-          else mbar_arrive(acc_empty);
+          if (CG == 2 && rank != 0) mbar_arrive_cluster(acc_empty_l + ab * 8);
+          else mbar_arrive(acc_empty + ab);
         }
 #pragma unroll
         for (int bx = 0; bx < 2; ++bx) {
@@ -984,8 +991,8 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {                           // drained: the next tile's MMAs may start
-          if (CG == 2 && rank != 0) mbar_arrive_cluster(acc_empty_l);
-          else mbar_arrive(acc_empty);
+          if (CG == 2 && rank != 0) mbar_arrive_cluster(acc_empty_l + ab * 8);
+          else mbar_arrive(acc_empty + ab);
         }
         if constexpr (MODE == MODE_FP4_QKV) {
           // this warp's 128 columns are head `head` of part q / k / v; thread = one row of it
@@ -1049,7 +1056,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
             }
           }
           __syncwarp();
-          acc_ph ^= 1;
+          ++acc_t;
           continue;
         }
         if constexpr (MODE == MODE_FP4_TP) {
@@ -1082,7 +1089,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
               __syncwarp();
             }
             sig_hand_off();                        // the signal warp tells the owner
-            acc_ph ^= 1;
+            ++acc_t;
             continue;
           }
           // this rank's rows: every other rank's partial of the tile has arrived in this rank's receive slots
@@ -1210,7 +1217,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
         }
         if constexpr (MODE == MODE_FP4_TP) sig_hand_off();   // own tile: the signal warp tells every other rank
       }
-      acc_ph ^= 1;
+      ++acc_t;
     }
     if (kResidMode && x_pending) {     // left the loop with a residual box still in flight
       const uint32_t a = smem_u32(xb);
