@@ -23,6 +23,8 @@
 //                   it to the MMA thread, then scale / convert / store while the next tile's MMAs run. bf16 outputs
 //                   go through a 128-byte-swizzled smem box per warp and TMA tensor stores: per-row 16-byte global
 //                   stores crowd the memory-instruction path the MMA issue shares and stalled it ~4500 cycles/tile.
+//                   FP8 keeps no scales in TMEM, so its accumulator is double-buffered (tile t in columns
+//                   256 * (t % 2)) and the next tile's MMAs do not wait for the drain.
 // Every mbarrier wait is bounded (kWaitLimitNs); a wait that runs out records a code in the device error word,
 // the other roles see it and leave their loops, in-flight copies/MMAs are drained (bounded) and TMEM is freed.
 // Each CTA issues its own tile loads from this GPU's memory; no load is broadcast across the cluster.
