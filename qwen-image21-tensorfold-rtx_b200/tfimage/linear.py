@@ -145,12 +145,15 @@ class Fp8Linear(Linear):
     def __init__(self, w: torch.Tensor, act: float | None = None, per_channel: bool = False):
         w = w.float()
         self.n, self.k = w.shape
+        # the reference's expressions, with the divisor as a tensor so that CUDA divides exactly (a Python-number
+        # divisor takes a reciprocal-multiply path there): scales and codes then equal the reference's on the CPU
+        e4m3_max = torch.tensor(E4M3_MAX, dtype=torch.float32, device=w.device)
         if per_channel:
-            s = (w.abs().amax(dim=1) / E4M3_MAX).clamp_min(1e-12)
+            s = (w.abs().amax(dim=1) / e4m3_max).clamp_min(1e-12)
             self.w8 = (w / s[:, None]).to(torch.float8_e4m3fn).contiguous()
             self.ws = s.contiguous()
         else:
-            s = (w.abs().amax() / E4M3_MAX).clamp_min(1e-12)
+            s = (w.abs().amax() / e4m3_max).clamp_min(1e-12)
             self.w8 = (w / s).to(torch.float8_e4m3fn).contiguous()
             self.ws = s.view(()).contiguous()
         self.act = act

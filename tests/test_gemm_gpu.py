@@ -205,15 +205,16 @@ def test_swiglu_mlp_api_and_fallback_contract(dev):
 
 
 def test_fp8_linear_api(dev):
-    """Fp8Linear end to end: its weight conversion is the reference's own torch code (run on the GPU, where torch's
-    divide-by-Python-scalar takes a reciprocal path, so a few w8 bytes may sit one e4m3 step from the numpy CPU
-    restatement); the activation quantizer and GEMM are checked against the oracle on the layer's own w8/ws."""
+    """Fp8Linear end to end: the weight conversion (the reference's torch expressions with tensor divisors, exact on
+    the GPU too) gives the oracle's w8 bytes and scales bit for bit; the activation quantizer and GEMM are checked
+    against the oracle on the layer's own w8/ws."""
     w = bf16_cpu((256, 384), seed=51, scale=0.02)
     x = bf16_cpu((100, 384), seed=52)
     for act, pc in ((None, False), (0.05, False), (None, True)):
         lin = L.Fp8Linear(w.to(dev), act, per_channel=pc)
-        w8_ref, _ = ofp8.weight(w.float().numpy(), pc)
-        assert (u8(lin.w8) == w8_ref).mean() > 0.99
+        w8_ref, ws_ref = ofp8.weight(w.float().numpy(), pc)
+        np.testing.assert_array_equal(u8(lin.w8), w8_ref)
+        np.testing.assert_array_equal(lin.ws.cpu().numpy(), ws_ref)
         y = lin(x.to(dev))
         ref = ofp8.linear(x.float().numpy(), u8(lin.w8), lin.ws.cpu().numpy(), act)
         assert rel_l2(f32(y), ref) <= TOL_FP8
