@@ -806,14 +806,18 @@ def run_ours(args):
             barrier()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            for (kind,) in ops:
-                st_ = s_in if kind == "in" else s_out
+            # every copy stream forks from the same point before any joins back, so "both" runs the two
+            # directions concurrently (joining after each copy would serialise them)
+            used = [s_in if kind == "in" else s_out for (kind,) in ops]
+            for st_ in used:
                 st_.wait_stream(stream)
+            for (kind,), st_ in zip(ops, used):
                 with torch.cuda.stream(st_):
                     if kind == "in":
                         x.copy_(x_host, non_blocking=True)
                     else:
                         y_host.copy_(y_dev, non_blocking=True)
+            for st_ in used:
                 stream.wait_stream(st_)
             b.record(stream)
             evs.append((a, b))
