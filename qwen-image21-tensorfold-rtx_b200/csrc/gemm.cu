@@ -1023,8 +1023,10 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
           }
           __nv_bfloat16* dst = p.qk_dst[part] + (int64_t)bb * p.qk_sb[part] + (int64_t)head * 128;
           const float* w = sSC + (part == 1 ? 128 : 0);
+          const int ck = lane & 7;
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
+            const int jj = c * 8 + ck;             // this lane's 8 columns of the head: RoPE pairs jj*4 .. jj*4+3
             __syncwarp();
 #pragma unroll
             for (int ch = 0; ch < 8; ++ch)
@@ -1034,27 +1036,39 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
             __syncwarp();
             // 4 rows x 128 B per pass: lane (r % 4) * 8 + ck takes chunk ck (8 values) of row r, so the row's cos /
             // sin (fp32, 64 per token) and the stores into the part's destination rows are both contiguous per 8
-            // lanes; the row's RMS factor comes from the lane that summed it
-#pragma unroll 2
-            for (int i = 0; i < 8; ++i) {
-              const int r = i * 4 + (lane >> 3), ck = lane & 7;
-              const float rr_r = __shfl_sync(0xffffffffu, rr, r);
-              const bool row_live = grow0 + r < p.M;
-              uint4 o = *reinterpret_cast<const uint4*>(stg + r * 128 + ((ck ^ (r & 7)) << 4));
-              if (part < 2 && row_live) {
-                float x[8];
-                unpack_bf16x8(o, x);
-                const int jj = c * 8 + ck;
-                const float4 w0 = *reinterpret_cast<const float4*>(w + jj * 8);
-                const float4 w1 = *reinterpret_cast<const float4*>(w + jj * 8 + 4);
-                const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.qk_cos + (int64_t)(n0 + r) * 64 + jj * 4));
-                const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.qk_sin + (int64_t)(n0 + r) * 64 + jj * 4));
-                const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-                const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
-                o = norm_rope8(x, rr_r, wv, cv, sv);
+            // lanes; the row's RMS factor comes from the lane that summed it. The cos / sin of four passes are
+            // loaded together, ahead of their math: token n0 + r < qk_ntok for every row of the warp, live or past
+            // M (M = B * qk_ntok and qk_ntok % 32 == 0), so the loads need no row guard
+#pragma unroll
+            for (int g4 = 0; g4 < 2; ++g4) {
+              float4 cq[4], sq[4];
+              if (part < 2) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  const int64_t t = (int64_t)(n0 + (g4 * 4 + u) * 4 + (lane >> 3)) * 64 + jj * 4;
+                  cq[u] = __ldg(reinterpret_cast<const float4*>(p.qk_cos + t));
+                  sq[u] = __ldg(reinterpret_cast<const float4*>(p.qk_sin + t));
+                }
               }
-              if (row_live && n_base + c * 64 < p.N)
-                *reinterpret_cast<uint4*>(dst + (int64_t)(n0 + r) * p.qk_sn[part] + c * 64 + ck * 8) = o;
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int r = (g4 * 4 + u) * 4 + (lane >> 3);
+                const float rr_r = __shfl_sync(0xffffffffu, rr, r);
+                const bool row_live = grow0 + r < p.M;
+                uint4 o = *reinterpret_cast<const uint4*>(stg + r * 128 + ((ck ^ (r & 7)) << 4));
+                if (part < 2 && row_live) {
+                  float x[8];
+                  unpack_bf16x8(o, x);
+                  const float4 w0 = *reinterpret_cast<const float4*>(w + jj * 8);
+                  const float4 w1 = *reinterpret_cast<const float4*>(w + jj * 8 + 4);
+                  const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                  const float cv[4] = {cq[u].x, cq[u].y, cq[u].z, cq[u].w};
+                  const float sv[4] = {sq[u].x, sq[u].y, sq[u].z, sq[u].w};
+                  o = norm_rope8(x, rr_r, wv, cv, sv);
+                }
+                if (row_live && n_base + c * 64 < p.N)
+                  *reinterpret_cast<uint4*>(dst + (int64_t)(n0 + r) * p.qk_sn[part] + c * 64 + ck * 8) = o;
+              }
             }
           }
           __syncwarp();
