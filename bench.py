@@ -766,7 +766,9 @@ def run_ours(args):
     events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     # After a barrier the GPU is idle and the first steps' windows would also hold the host's time to queue their
     # kernels; a ~2 ms GPU sleep ahead of each pass (outside every event window) lets the host queue them first.
-    lead = lambda: torch.cuda._sleep(4_000_000)                                  # noqa: E731 -- cycles
+    def lead():
+        if hasattr(torch.cuda, "_sleep"):                 # torch's spin kernel (cycles); without it: no lead
+            torch.cuda._sleep(4_000_000)
     barrier()
     with ClockSampler(local) as clk:
         lead()
